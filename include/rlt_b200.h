@@ -1,0 +1,160 @@
+/* C ABI of the B200 (sm_100a) paged-KV attention path of a looped
+ * (recurrent-depth) transformer.
+ *
+ * Every entry point takes plain device pointers, element counts and element
+ * strides (in elements, not bytes), launches on the given CUDA stream and
+ * returns immediately: no host synchronisation, no allocation, so each call
+ * can be captured into a CUDA graph. Scratch memory (split-KV partials) is
+ * passed in by the caller; its size comes from the matching *_bytes query.
+ *
+ * Return value: RLT_OK (0), a negative RLT_E* code for an invalid argument
+ * (nothing was launched), or a positive cudaError_t from the launch.
+ *
+ * Data layouts follow the reference engine (vllm_rlt):
+ *   KV pool      [num_blocks, num_layers, page, num_kv_heads, head_dim]
+ *                (vllm_rlt/core/kv_cache_manager.py:132-134); attention takes
+ *                the layer view [num_blocks, page, num_kv_heads, head_dim]
+ *                whose block stride is num_layers*page*num_kv_heads*head_dim.
+ *   block tables int32 [rows, width], padded with -1 (or 0 in static buffers).
+ *   lengths      int32 [rows], 0 for padding rows.
+ *   q / out      [rows, num_q_heads, head_dim].
+ * The last (head_dim) dimension of q, out, K and V must be contiguous.
+ *
+ * status (optional, may be NULL): an int32 device word that kernels OR error
+ * bits into when metadata points outside the pool (RLT_STATUS_*). The bad
+ * page/row is skipped instead of being dereferenced.
+ */
+#ifndef RLT_B200_H_
+#define RLT_B200_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* element type codes */
+#define RLT_F32 0
+#define RLT_F16 1
+#define RLT_BF16 2
+
+/* return codes */
+#define RLT_OK 0
+#define RLT_E_DTYPE -1
+#define RLT_E_HEAD_DIM -2
+#define RLT_E_HEADS -3
+#define RLT_E_WORKSPACE -4
+#define RLT_E_SHAPE -5
+#define RLT_E_ALIGN -6
+#define RLT_E_DEVICE -7
+
+/* status bits */
+#define RLT_STATUS_BAD_LENGTH 1
+#define RLT_STATUS_BAD_BLOCK 2
+#define RLT_STATUS_BAD_OFFSET 4
+#define RLT_STATUS_BAD_SLOT 8
+#define RLT_STATUS_BAD_SEQUENCE 16
+
+/* Library version (major*10000 + minor*100 + patch). */
+int rlt_version(void);
+
+/* Bytes of scratch rlt_paged_decode needs for this launch shape: fp32
+ * split-KV partials (acc, running max, normaliser) for every row, query head
+ * and split. 0 when no row can need more than one split. */
+size_t rlt_paged_decode_workspace_bytes(int32_t num_rows, int32_t num_q_heads, int32_t head_dim,
+                                        int32_t page_size, int32_t table_width);
+
+/* Depth-aware paged decode attention: one query token per row, each row with
+ * its own block table (the row's depth plane already selected by the caller),
+ * GQA, fp32 softmax/accumulation, output in the input dtype.
+ *   out[r, h] = softmax(q[r, h] . K[r, :len_r, h/g]^T * scale) V[r, :len_r, h/g]
+ * with K[r, t] = key_cache[block_tables[r, t / page], t % page]; len_r = 0
+ * rows produce zeros.
+ * Replaces: vllm_rlt/kernels/triton_attention.py:100-125 (paged_attention,
+ * Triton kernel :13-97), the FA4 decode call at
+ * vllm_rlt/kernels/flash_attention.py:98-130, and the oracle
+ * vllm_rlt/kernels/paged_attention.py:12-36 (torch_paged_attention). */
+int rlt_paged_decode(const void* q, const void* key_cache, const void* value_cache,
+                     const int32_t* block_tables, const int32_t* context_lengths, void* out,
+                     void* workspace, size_t workspace_bytes, int32_t* status, int32_t dtype,
+                     int32_t num_rows, int32_t num_q_heads, int32_t num_kv_heads,
+                     int32_t head_dim, int32_t page_size, int32_t table_width,
+                     int64_t num_blocks, int64_t q_row_stride, int64_t q_head_stride,
+                     int64_t k_block_stride, int64_t k_token_stride, int64_t k_head_stride,
+                     int64_t v_block_stride, int64_t v_token_stride, int64_t v_head_stride,
+                     int64_t table_row_stride, int64_t out_row_stride, int64_t out_head_stride,
+                     float scale, void* stream);
+
+/* KV page write into the depth plane (reshape_and_cache):
+ *   key_cache[write_blocks[i], layer, write_offsets[i]] = k[i]   (i < num_rows)
+ *   value_cache[...]                                    = v[i]
+ * Bit-exact copy. Pool strides are those of the 5-D pool.
+ * Replaces: vllm_rlt/core/kv_cache_manager.py:531-532 (_write_prepared) and
+ * the graph-captured copy at vllm_rlt/worker/cuda_graph.py:16-19. */
+int rlt_kv_write(const void* k, const void* v, void* key_cache, void* value_cache,
+                 const int64_t* write_blocks, const int64_t* write_offsets, int32_t* status,
+                 int32_t dtype, int32_t num_rows, int32_t num_kv_heads, int32_t head_dim,
+                 int32_t layer, int32_t page_size, int64_t num_blocks, int64_t k_row_stride,
+                 int64_t k_head_stride, int64_t v_row_stride, int64_t v_head_stride,
+                 int64_t cache_block_stride, int64_t cache_layer_stride,
+                 int64_t cache_token_stride, int64_t cache_head_stride, void* stream);
+
+/* LAST-EXITED exit copy: for each descriptor row (slot, depth, pos) copy the
+ * token's K and V of every layer from plane `depth` into every deeper plane
+ * (depth, planes), through the resident tables[slot, plane, width].
+ * descriptor may be a mapped (UVA) pinned host pointer. Bit-exact.
+ * Replaces: vllm_rlt/kernels/routing.py:79-109 (finalize_kernel, launched at
+ * vllm_rlt/worker/model_runner.py:543-557) and the eager copies of
+ * vllm_rlt/core/kv_cache_manager.py:601-611 (finalize_token). */
+int rlt_finalize(const int64_t* descriptor, const int32_t* tables, void* key_cache,
+                 void* value_cache, int32_t* status, int32_t dtype, int32_t num_rows,
+                 int32_t num_slots, int32_t width, int32_t planes, int32_t page_size,
+                 int32_t num_layers, int32_t channels, int64_t num_blocks,
+                 int64_t block_stride, int64_t layer_stride, int64_t token_stride, void* stream);
+
+/* Depth/page resolution of one routing bank: descriptor rows (slot, depth,
+ * pos) -> slots, positions, lengths = pos + 1 (0 for rows >= n), write block /
+ * offset, and the row's depth-plane table copied into out_tables[row, :out_width]
+ * (row stride `width`). Rows in [n, size) are padding.
+ * Replaces: vllm_rlt/kernels/routing.py:7-41 (metadata_kernel, launched at
+ * vllm_rlt/worker/async_state.py:181-197). */
+int rlt_metadata(const int64_t* descriptor, const int32_t* tables, int64_t* slots,
+                 int64_t* positions, int32_t* lengths, int64_t* blocks, int64_t* offsets,
+                 int32_t* out_tables, int32_t* status, int32_t n, int32_t size, int32_t width,
+                 int32_t page_size, int32_t planes, int32_t out_width, int32_t num_slots,
+                 void* stream);
+
+/* Copy a (mapped pinned or device) int64 metadata bank to device int64 and
+ * int32 copies. Replaces: vllm_rlt/kernels/prefill_metadata.py:7-12
+ * (stage_prefill, launched at vllm_rlt/worker/prefill_metadata.py:53-55). */
+int rlt_stage_prefill(const int64_t* source, int64_t* target, int32_t* target32, int64_t n,
+                      void* stream);
+
+/* Per packed-prefill token: block = tables[seq * width + pos / page],
+ * offset = pos % page. Replaces: vllm_rlt/kernels/prefill_metadata.py:15-32
+ * (expand_prefill, launched at vllm_rlt/worker/prefill_metadata.py:75-86). */
+int rlt_expand_prefill(const int64_t* positions, const int64_t* sequences, const int32_t* tables,
+                       int64_t* blocks, int64_t* offsets, int32_t* status, int64_t n,
+                       int32_t width, int32_t page_size, int64_t num_table_entries,
+                       void* stream);
+
+/* Resident-slot gather: out[row, :] = pool[slots[row], :] for row < n, zeros
+ * for n <= row < size. elem_bytes in {1, 2, 4, 8}; strides in elements.
+ * Replaces: vllm_rlt/kernels/routing.py:44-59 (gather_kernel, launched at
+ * vllm_rlt/worker/async_state.py:215-224). */
+int rlt_gather(const void* pool, const int64_t* slots, void* out, int32_t n, int32_t size,
+               int32_t width, int32_t elem_bytes, int64_t in_stride, int64_t out_stride,
+               void* stream);
+
+/* Resident-slot scatter: pool[slots[row], :] = values[row, :] for row < n.
+ * Replaces: vllm_rlt/kernels/routing.py:62-76 (scatter_kernel, launched at
+ * vllm_rlt/worker/async_state.py:226-234). */
+int rlt_scatter(const void* values, const int64_t* slots, void* pool, int32_t n, int32_t width,
+                int32_t elem_bytes, int64_t in_stride, int64_t out_stride, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* RLT_B200_H_ */

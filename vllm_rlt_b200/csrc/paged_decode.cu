@@ -1,0 +1,600 @@
+// Depth-aware paged decode attention for sm_100a.
+//
+// Semantics (vllm_rlt/kernels/paged_attention.py:12-36, the reference's torch
+// oracle, and the Triton kernel vllm_rlt/kernels/triton_attention.py:13-97):
+// every row r has one query token, its own block table (the caller already
+// picked the row's depth plane) and a context length len_r; for query head h
+//   out[r, h] = softmax_t(q[r, h] . K[t, h / group] * scale) . V[t, h / group]
+// over t < len_r, K[t] = key_cache[table[r, t / page], t % page]. fp32 math,
+// output in the input dtype, len_r = 0 gives zeros.
+//
+// Mapping (HBM-bound: every K/V byte is read exactly once per kv head):
+//  * grid.x = row x (tasks of the row / warps per CTA), grid.y = split;
+//  * a warp task is one kv head with GC query heads of its GQA group, over
+//    one split (a contiguous token range) of the row;
+//  * LPT = head_dim / (16 B / elt) lanes read one token's 16-byte-aligned
+//    head row with one 16-byte load each, so a warp-wide load covers
+//    32 / LPT whole token rows (fully used 32-byte sectors);
+//  * every lane accumulates dot-product partials for TOK tokens, then a
+//    butterfly reduce-scatter (TOK - 1 shuffles) leaves each lane holding the
+//    full score of one token; online softmax runs per warp iteration;
+//  * probabilities go through a per-warp shared buffer so that each lane can
+//    apply them to its own slice of the V rows it loaded;
+//  * long rows are split; each split writes an fp32 (acc, max, sum) partial
+//    and a combine kernel merges them. The split plan is a function of the
+//    row's own length only, so results are batch-invariant.
+#include "common.cuh"
+
+namespace rlt {
+namespace {
+
+constexpr int kDecodeWarps = 4;     // warps (= warp tasks) per CTA
+constexpr int kSplitAlign = 32;     // every split starts at a multiple of this
+constexpr int kSplitChunk = 256;    // target tokens per split
+constexpr int kMaxSplits = 32;      // cap; longer rows get longer splits
+
+struct DecodeParams {
+  const void* q;
+  const void* k;
+  const void* v;
+  const int32_t* tables;
+  const int32_t* lengths;
+  void* out;
+  float* ws_o;   // [rows, launch_splits, hq, head_dim] unnormalised acc
+  float* ws_ml;  // [rows, launch_splits, hq, 2] (running max in log2 units, sum)
+  int32_t* status;
+  int rows, hq, hkv, group, head_dim, page, width, launch_splits;
+  int64_t num_blocks;
+  int64_t q_rs, q_hs, k_bs, k_ts, k_hs, v_bs, v_ts, v_hs, t_rs, o_rs, o_hs;
+  float scale_log2;  // softmax scale * log2(e): scores are kept in base 2
+};
+
+struct SplitPlan {
+  int count;  // number of non-empty splits
+  int per;    // tokens per split (multiple of kSplitAlign)
+};
+
+// A function of the row's own length only (never of the batch or the launch
+// shape), which keeps every row's reduction order batch-invariant.
+__host__ __device__ __forceinline__ SplitPlan split_plan(int ctx) {
+  if (ctx <= 0) return {0, 0};
+  int n = (ctx + kSplitChunk - 1) / kSplitChunk;
+  if (n > kMaxSplits) n = kMaxSplits;
+  int per = (ctx + n - 1) / n;
+  per = (per + kSplitAlign - 1) / kSplitAlign * kSplitAlign;
+  return {(ctx + per - 1) / per, per};
+}
+
+__host__ __device__ __forceinline__ int launch_splits_for(int64_t max_ctx) {
+  if (max_ctx <= 0) return 1;
+  int64_t n = (max_ctx + kSplitChunk - 1) / kSplitChunk;
+  return n > kMaxSplits ? kMaxSplits : static_cast<int>(n);
+}
+
+// Tokens each lane group covers per warp iteration: as many as the lanes of
+// a token row (so a full reduce-scatter ends with one token per lane), capped
+// so that TOK partials for GC query heads stay in registers.
+__host__ __device__ constexpr int tokens_per_group(int lpt, int gc) {
+  return lpt < 16 / gc ? lpt : 16 / gc;
+}
+
+template <int N>
+struct Log2 {
+  static constexpr int value = 1 + Log2<N / 2>::value;
+};
+template <>
+struct Log2<1> {
+  static constexpr int value = 0;
+};
+
+// Length of row `row`, clamped to what its table can address.
+__device__ __forceinline__ int checked_length(const DecodeParams& p, int row, bool report) {
+  int ctx = p.lengths[row];
+  if (ctx < 0 || static_cast<int64_t>(ctx) > static_cast<int64_t>(p.width) * p.page) {
+    if (report) raise_status(p.status, kStatusBadLength);
+    return 0;
+  }
+  return ctx;
+}
+
+template <typename T, int D, int GC, bool ALIGNED>
+__global__ void __launch_bounds__(kDecodeWarps * 32, 4)
+    paged_decode_kernel(const __grid_constant__ DecodeParams p) {
+  constexpr int VEC = Vec16<T>::kElems;
+  constexpr int LPT = D / VEC;  // lanes per token row
+  static_assert(LPT >= 4 && LPT <= 32 && (LPT & (LPT - 1)) == 0, "unsupported head_dim");
+  constexpr int GROUPS = 32 / LPT;       // token rows per warp-wide load
+  constexpr int TOK = tokens_per_group(LPT, GC);  // tokens per lane group per iteration
+  constexpr int ITOK = GROUPS * TOK;     // tokens per warp iteration
+  constexpr int RS = Log2<TOK>::value;   // reduce-scatter steps
+  constexpr int PLAIN = Log2<LPT / TOK>::value;  // remaining plain reduction steps
+  static_assert(kSplitAlign % ITOK == 0, "split alignment must cover a warp iteration");
+
+  __shared__ __align__(16) float pbuf[kDecodeWarps][GC][ITOK];
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int qchunks = p.group / GC;
+  const int tasks_per_row = p.hkv * qchunks;
+  const int blocks_per_row = (tasks_per_row + kDecodeWarps - 1) / kDecodeWarps;
+  const int row = blockIdx.x / blocks_per_row;
+  const int task = (blockIdx.x - row * blocks_per_row) * kDecodeWarps + warp;
+  const int split = blockIdx.y;
+  if (task >= tasks_per_row) return;
+  const int kvh = task / qchunks;
+  const int qh0 = kvh * p.group + (task - kvh * qchunks) * GC;
+
+  const int g = lane / LPT;  // lane group: which token row of a warp-wide load
+  const int s = lane % LPT;  // 16-byte slice of the head row
+  T* out = static_cast<T*>(p.out);
+
+  const int ctx = checked_length(p, row, split == 0 && task == 0 && lane == 0);
+  if (ctx == 0) {
+    if (split == 0 && g == 0) {
+      const float zero[VEC] = {};
+#pragma unroll
+      for (int c = 0; c < GC; ++c)
+        st_vec(out + row * p.o_rs + (qh0 + c) * p.o_hs + s * VEC, pack16<T>(zero));
+    }
+    return;
+  }
+  const SplitPlan plan = split_plan(ctx);
+  if (split >= plan.count) return;
+  const int start = split * plan.per;
+  const int end = min(ctx, start + plan.per);
+
+  // Query slice, pre-scaled into base-2 logits.
+  float qf[GC][VEC];
+#pragma unroll
+  for (int c = 0; c < GC; ++c) {
+    const T* qp = static_cast<const T*>(p.q) + row * p.q_rs + (qh0 + c) * p.q_hs + s * VEC;
+    unpack16<T>(ld_vec(qp), qf[c]);
+#pragma unroll
+    for (int e = 0; e < VEC; ++e) qf[c][e] *= p.scale_log2;
+  }
+
+  float acc[GC][VEC];
+  float m[GC], lsum[GC];
+#pragma unroll
+  for (int c = 0; c < GC; ++c) {
+    m[c] = -INFINITY;
+    lsum[c] = 0.f;
+#pragma unroll
+    for (int e = 0; e < VEC; ++e) acc[c][e] = 0.f;
+  }
+
+  const T* kbase = static_cast<const T*>(p.k) + kvh * p.k_hs + s * VEC;
+  const T* vbase = static_cast<const T*>(p.v) + kvh * p.v_hs + s * VEC;
+  const int32_t* trow = p.tables + row * p.t_rs;
+  const int tl = s >> PLAIN;  // token (within the group) whose score this lane ends with
+  const bool writer = (s & ((1 << PLAIN) - 1)) == 0;
+  const uint4 zero4 = make_uint4(0, 0, 0, 0);
+
+  for (int base = start; base < end; base += ITOK) {
+    const int t0 = base + g * TOK;  // first token of this lane group
+    uint4 kr[TOK];
+    bool page_ok = false;
+    int64_t kp = 0, vp = 0;  // aligned path: element offsets of token t0's page row
+    int64_t my_k = -1, my_v = 0;  // generic path: offsets of token t0 + s (lane s < TOK)
+    if constexpr (ALIGNED) {
+      // page % TOK == 0 and t0 % TOK == 0: the group's TOK tokens share a page.
+      if (t0 < end) {
+        const int blk = __ldg(trow + t0 / p.page);
+        if (blk >= 0 && blk < p.num_blocks) {
+          const int off = t0 % p.page;
+          kp = blk * p.k_bs + off * p.k_ts;
+          vp = blk * p.v_bs + off * p.v_ts;
+          page_ok = true;
+        } else if (s == 0) {
+          raise_status(p.status, kStatusBadBlock);
+        }
+      }
+#pragma unroll
+      for (int j = 0; j < TOK; ++j)
+        kr[j] = (page_ok && t0 + j < end) ? ld_stream(kbase + kp + j * p.k_ts) : zero4;
+    } else {
+      if (s < TOK) {
+        const int t = t0 + s;
+        if (t < end) {
+          const int blk = __ldg(trow + t / p.page);
+          if (blk >= 0 && blk < p.num_blocks) {
+            my_k = blk * p.k_bs + (t % p.page) * p.k_ts;
+            my_v = blk * p.v_bs + (t % p.page) * p.v_ts;
+          } else {
+            raise_status(p.status, kStatusBadBlock);
+          }
+        }
+      }
+#pragma unroll
+      for (int j = 0; j < TOK; ++j) {
+        const int64_t kj = __shfl_sync(kFullMask, my_k, g * LPT + j);
+        kr[j] = kj >= 0 ? ld_stream(kbase + kj) : zero4;
+      }
+    }
+
+    // Dot-product partials over this lane's VEC dims for each of TOK tokens.
+    float part[GC][TOK];
+#pragma unroll
+    for (int j = 0; j < TOK; ++j) {
+      float kf[VEC];
+      unpack16<T>(kr[j], kf);
+#pragma unroll
+      for (int c = 0; c < GC; ++c) {
+        float a = 0.f;
+#pragma unroll
+        for (int e = 0; e < VEC; ++e) a = fmaf(qf[c][e], kf[e], a);
+        part[c][j] = a;
+      }
+    }
+
+    // Issue the V loads now so they overlap the reductions below.
+    uint4 vr[TOK];
+    if constexpr (ALIGNED) {
+#pragma unroll
+      for (int j = 0; j < TOK; ++j)
+        vr[j] = (page_ok && t0 + j < end) ? ld_stream(vbase + vp + j * p.v_ts) : zero4;
+    } else {
+#pragma unroll
+      for (int j = 0; j < TOK; ++j) {
+        const int64_t kj = __shfl_sync(kFullMask, my_k, g * LPT + j);
+        const int64_t vj = __shfl_sync(kFullMask, my_v, g * LPT + j);
+        vr[j] = kj >= 0 ? ld_stream(vbase + vj) : zero4;
+      }
+    }
+
+    // Butterfly reduce-scatter across the LPT lanes of the group: after step
+    // k each lane keeps half of its partials, so lane s ends with token s>>PLAIN.
+#pragma unroll
+    for (int c = 0; c < GC; ++c) {
+#pragma unroll
+      for (int step = 0; step < RS; ++step) {
+        const int n = TOK >> step;
+        const int mask = LPT >> (step + 1);
+        const bool upper = (lane & mask) != 0;
+#pragma unroll
+        for (int j = 0; j < n / 2; ++j) {
+          const float send = upper ? part[c][j] : part[c][j + n / 2];
+          const float keep = upper ? part[c][j + n / 2] : part[c][j];
+          part[c][j] = keep + __shfl_xor_sync(kFullMask, send, mask);
+        }
+      }
+#pragma unroll
+      for (int step = 0; step < PLAIN; ++step) {
+        const int mask = (LPT / TOK) >> (step + 1);
+        part[c][0] += __shfl_xor_sync(kFullMask, part[c][0], mask);
+      }
+    }
+
+    bool valid;
+    if constexpr (ALIGNED) {
+      valid = page_ok && (t0 + tl) < end;
+    } else {
+      valid = __shfl_sync(kFullMask, my_k, g * LPT + tl) >= 0;
+    }
+
+    // Online softmax (base 2) over the warp's ITOK tokens.
+#pragma unroll
+    for (int c = 0; c < GC; ++c) {
+      const float sc = valid ? part[c][0] : -INFINITY;
+      float mt = sc;
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) mt = fmaxf(mt, __shfl_xor_sync(kFullMask, mt, o));
+      const float mnew = fmaxf(m[c], mt);
+      const float mref = mnew == -INFINITY ? 0.f : mnew;
+      const float corr = ex2(m[c] - mref);
+      const float pr = ex2(sc - mref);
+      m[c] = mnew;
+      lsum[c] = lsum[c] * corr + (writer ? pr : 0.f);
+#pragma unroll
+      for (int e = 0; e < VEC; ++e) acc[c][e] *= corr;
+      if (writer) pbuf[warp][c][g * TOK + tl] = pr;
+    }
+    __syncwarp();
+
+#pragma unroll
+    for (int c = 0; c < GC; ++c) {
+      float pj[TOK];
+#pragma unroll
+      for (int j = 0; j < TOK; j += 4) {
+        const float4 w = *reinterpret_cast<const float4*>(&pbuf[warp][c][g * TOK + j]);
+        pj[j] = w.x;
+        pj[j + 1] = w.y;
+        pj[j + 2] = w.z;
+        pj[j + 3] = w.w;
+      }
+#pragma unroll
+      for (int j = 0; j < TOK; ++j) {
+        float vf[VEC];
+        unpack16<T>(vr[j], vf);
+#pragma unroll
+        for (int e = 0; e < VEC; ++e) acc[c][e] = fmaf(pj[j], vf[e], acc[c][e]);
+      }
+    }
+    __syncwarp();
+  }
+
+  // Merge the lane groups (they covered different tokens of the same dims).
+#pragma unroll
+  for (int c = 0; c < GC; ++c) {
+#pragma unroll
+    for (int o = LPT; o < 32; o <<= 1) {
+#pragma unroll
+      for (int e = 0; e < VEC; ++e) acc[c][e] += __shfl_xor_sync(kFullMask, acc[c][e], o);
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) lsum[c] += __shfl_xor_sync(kFullMask, lsum[c], o);
+  }
+
+  if (plan.count == 1) {
+    if (g == 0) {
+#pragma unroll
+      for (int c = 0; c < GC; ++c) {
+        const float inv = 1.f / fmaxf(lsum[c], 1e-30f);
+        float o[VEC];
+#pragma unroll
+        for (int e = 0; e < VEC; ++e) o[e] = acc[c][e] * inv;
+        st_vec(out + row * p.o_rs + (qh0 + c) * p.o_hs + s * VEC, pack16<T>(o));
+      }
+    }
+    return;
+  }
+  const int64_t slot = (static_cast<int64_t>(row) * p.launch_splits + split) * p.hq + qh0;
+  if (g == 0) {
+#pragma unroll
+    for (int c = 0; c < GC; ++c) {
+      float* dst = p.ws_o + (slot + c) * p.head_dim + s * VEC;
+#pragma unroll
+      for (int e = 0; e < VEC; e += 4)
+        *reinterpret_cast<float4*>(dst + e) =
+            make_float4(acc[c][e], acc[c][e + 1], acc[c][e + 2], acc[c][e + 3]);
+    }
+  }
+  if (lane == 0) {
+#pragma unroll
+    for (int c = 0; c < GC; ++c)
+      *reinterpret_cast<float2*>(p.ws_ml + (slot + c) * 2) = make_float2(m[c], lsum[c]);
+  }
+}
+
+// Merge the split partials of rows that needed more than one split.
+// grid = (rows, hq), block = head_dim threads (rounded up to a warp).
+template <typename T>
+__global__ void __launch_bounds__(256) decode_combine_kernel(const __grid_constant__ DecodeParams p) {
+  const int row = blockIdx.x;
+  const int qh = blockIdx.y;
+  const int ctx = checked_length(p, row, false);
+  const SplitPlan plan = split_plan(ctx);
+  if (plan.count <= 1) return;
+  const int64_t base = static_cast<int64_t>(row) * p.launch_splits * p.hq + qh;
+  float mx = -INFINITY;
+  for (int sp = 0; sp < plan.count; ++sp) mx = fmaxf(mx, p.ws_ml[(base + sp * p.hq) * 2]);
+  const float mref = mx == -INFINITY ? 0.f : mx;
+  float total = 0.f;
+  for (int sp = 0; sp < plan.count; ++sp) {
+    const float2 ml = *reinterpret_cast<const float2*>(p.ws_ml + (base + sp * p.hq) * 2);
+    total += ml.y * ex2(ml.x - mref);
+  }
+  const float inv = 1.f / fmaxf(total, 1e-30f);
+  T* out = static_cast<T*>(p.out) + row * p.o_rs + qh * p.o_hs;
+  for (int d = threadIdx.x; d < p.head_dim; d += blockDim.x) {
+    float o = 0.f;
+    for (int sp = 0; sp < plan.count; ++sp) {
+      const float w = ex2(p.ws_ml[(base + sp * p.hq) * 2] - mref);
+      o = fmaf(p.ws_o[(base + sp * p.hq) * p.head_dim + d], w, o);
+    }
+    out[d] = from_f32<T>(o * inv);
+  }
+}
+
+// Any head_dim <= 256, any alignment: one warp per (row, query head), dims
+// spread over lanes, tokens in order. Used when the fast kernel's 16-byte
+// vector contract does not hold (odd head_dim, unaligned strides).
+template <typename T>
+__global__ void __launch_bounds__(128) paged_decode_generic_kernel(const __grid_constant__ DecodeParams p) {
+  const int lane = threadIdx.x & 31;
+  const int64_t wid = static_cast<int64_t>(blockIdx.x) * 4 + (threadIdx.x >> 5);
+  if (wid >= static_cast<int64_t>(p.rows) * p.hq) return;
+  const int row = static_cast<int>(wid / p.hq);
+  const int qh = static_cast<int>(wid % p.hq);
+  const int kvh = qh / p.group;
+  const int D = p.head_dim;
+  const int ctx = checked_length(p, row, qh == 0 && lane == 0);
+  const T* qp = static_cast<const T*>(p.q) + row * p.q_rs + qh * p.q_hs;
+  float qv[8], acc[8];
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const int d = lane + 32 * i;
+    qv[i] = d < D ? to_f32<T>(qp[d]) * p.scale_log2 : 0.f;
+    acc[i] = 0.f;
+  }
+  float m = -INFINITY, l = 0.f;
+  const int32_t* trow = p.tables + row * p.t_rs;
+  for (int t = 0; t < ctx; ++t) {
+    const int blk = __ldg(trow + t / p.page);
+    if (blk < 0 || blk >= p.num_blocks) {
+      if (lane == 0) raise_status(p.status, kStatusBadBlock);
+      continue;
+    }
+    const T* kp = static_cast<const T*>(p.k) + blk * p.k_bs + (t % p.page) * p.k_ts + kvh * p.k_hs;
+    const T* vp = static_cast<const T*>(p.v) + blk * p.v_bs + (t % p.page) * p.v_ts + kvh * p.v_hs;
+    float part = 0.f;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const int d = lane + 32 * i;
+      if (d < D) part = fmaf(qv[i], to_f32<T>(kp[d]), part);
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) part += __shfl_xor_sync(kFullMask, part, o);
+    const float mnew = fmaxf(m, part);
+    const float corr = ex2(m - mnew);
+    const float pr = ex2(part - mnew);
+    l = l * corr + pr;
+    m = mnew;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const int d = lane + 32 * i;
+      acc[i] = fmaf(pr, d < D ? to_f32<T>(vp[d]) : 0.f, acc[i] * corr);
+    }
+  }
+  T* op = static_cast<T*>(p.out) + row * p.o_rs + qh * p.o_hs;
+  const float inv = 1.f / fmaxf(l, 1e-30f);
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const int d = lane + 32 * i;
+    if (d < D) op[d] = from_f32<T>(acc[i] * inv);
+  }
+}
+
+template <typename T, int D, int GC>
+cudaError_t launch_fast(const DecodeParams& p, cudaStream_t stream) {
+  constexpr int VEC = Vec16<T>::kElems;
+  constexpr int LPT = D / VEC;
+  constexpr int TOK = tokens_per_group(LPT, GC);
+  const int tasks = p.hkv * (p.group / GC);
+  const int blocks_per_row = (tasks + kDecodeWarps - 1) / kDecodeWarps;
+  dim3 grid(static_cast<unsigned>(p.rows) * blocks_per_row, p.launch_splits);
+  if (p.page % TOK == 0)
+    paged_decode_kernel<T, D, GC, true><<<grid, kDecodeWarps * 32, 0, stream>>>(p);
+  else
+    paged_decode_kernel<T, D, GC, false><<<grid, kDecodeWarps * 32, 0, stream>>>(p);
+  cudaError_t err = cudaGetLastError();
+  if (err != cudaSuccess || p.launch_splits <= 1) return err;
+  decode_combine_kernel<T><<<dim3(p.rows, p.hq), D <= 256 ? D : 256, 0, stream>>>(p);
+  return cudaGetLastError();
+}
+
+template <typename T, int D>
+cudaError_t launch_gc(const DecodeParams& p, cudaStream_t stream) {
+  if (p.group % 2 == 0) return launch_fast<T, D, 2>(p, stream);
+  return launch_fast<T, D, 1>(p, stream);
+}
+
+template <typename T>
+cudaError_t launch_typed(DecodeParams p, bool fast, cudaStream_t stream) {
+  if (fast) {
+    switch (p.head_dim) {
+      case 32: return launch_gc<T, 32>(p, stream);
+      case 64: return launch_gc<T, 64>(p, stream);
+      case 128: return launch_gc<T, 128>(p, stream);
+      case 256:
+        if constexpr (sizeof(T) == 2) return launch_gc<T, 256>(p, stream);
+        break;
+      default: break;
+    }
+  }
+  p.launch_splits = 1;  // the generic kernel never splits
+  const int64_t warps = static_cast<int64_t>(p.rows) * p.hq;
+  paged_decode_generic_kernel<T><<<static_cast<unsigned>((warps + 3) / 4), 128, 0, stream>>>(p);
+  return cudaGetLastError();
+}
+
+bool aligned16(const void* ptr) { return (reinterpret_cast<uintptr_t>(ptr) & 15u) == 0; }
+
+int elem_size(int32_t dtype) {
+  switch (dtype) {
+    case RLT_F32: return 4;
+    case RLT_F16:
+    case RLT_BF16: return 2;
+    default: return 0;
+  }
+}
+
+// Whether the 16-byte vector kernel applies to this head_dim / dtype.
+bool fast_head_dim(int head_dim, int esize) {
+  if (esize == 2) return head_dim == 32 || head_dim == 64 || head_dim == 128 || head_dim == 256;
+  return head_dim == 32 || head_dim == 64 || head_dim == 128;
+}
+
+}  // namespace
+}  // namespace rlt
+
+using namespace rlt;
+
+extern "C" int rlt_version(void) { return 100; }
+
+extern "C" size_t rlt_paged_decode_workspace_bytes(int32_t num_rows, int32_t num_q_heads,
+                                                   int32_t head_dim, int32_t page_size,
+                                                   int32_t table_width) {
+  if (num_rows <= 0 || num_q_heads <= 0 || head_dim <= 0) return 0;
+  const int splits = launch_splits_for(static_cast<int64_t>(page_size) * table_width);
+  if (splits <= 1) return 0;
+  return static_cast<size_t>(num_rows) * splits * num_q_heads * (head_dim + 2) * sizeof(float);
+}
+
+extern "C" int rlt_paged_decode(const void* q, const void* key_cache, const void* value_cache,
+                                const int32_t* block_tables, const int32_t* context_lengths,
+                                void* out, void* workspace, size_t workspace_bytes,
+                                int32_t* status, int32_t dtype, int32_t num_rows,
+                                int32_t num_q_heads, int32_t num_kv_heads, int32_t head_dim,
+                                int32_t page_size, int32_t table_width, int64_t num_blocks,
+                                int64_t q_row_stride, int64_t q_head_stride,
+                                int64_t k_block_stride, int64_t k_token_stride,
+                                int64_t k_head_stride, int64_t v_block_stride,
+                                int64_t v_token_stride, int64_t v_head_stride,
+                                int64_t table_row_stride, int64_t out_row_stride,
+                                int64_t out_head_stride, float scale, void* stream) {
+  const int esize = elem_size(dtype);
+  if (esize == 0) return RLT_E_DTYPE;
+  if (head_dim <= 0 || head_dim > 256) return RLT_E_HEAD_DIM;
+  if (num_q_heads <= 0 || num_kv_heads <= 0 || num_q_heads % num_kv_heads) return RLT_E_HEADS;
+  if (num_rows < 0 || page_size <= 0 || table_width < 0 || num_blocks < 0) return RLT_E_SHAPE;
+  if (num_rows == 0) return RLT_OK;
+
+  DecodeParams p{};
+  p.q = q;
+  p.k = key_cache;
+  p.v = value_cache;
+  p.tables = block_tables;
+  p.lengths = context_lengths;
+  p.out = out;
+  p.status = status;
+  p.rows = num_rows;
+  p.hq = num_q_heads;
+  p.hkv = num_kv_heads;
+  p.group = num_q_heads / num_kv_heads;
+  p.head_dim = head_dim;
+  p.page = page_size;
+  p.width = table_width;
+  p.num_blocks = num_blocks;
+  p.q_rs = q_row_stride;
+  p.q_hs = q_head_stride;
+  p.k_bs = k_block_stride;
+  p.k_ts = k_token_stride;
+  p.k_hs = k_head_stride;
+  p.v_bs = v_block_stride;
+  p.v_ts = v_token_stride;
+  p.v_hs = v_head_stride;
+  p.t_rs = table_row_stride;
+  p.o_rs = out_row_stride;
+  p.o_hs = out_head_stride;
+  p.scale_log2 = scale * 1.4426950408889634f;
+
+  // The 16-byte vector contract: every base pointer and every stride that
+  // moves between head rows is a multiple of 16 bytes.
+  const int64_t vec = 16 / esize;
+  bool fast = fast_head_dim(head_dim, esize) && aligned16(q) && aligned16(key_cache) &&
+              aligned16(value_cache) && aligned16(out);
+  for (int64_t st : {q_row_stride, q_head_stride, k_block_stride, k_token_stride, k_head_stride,
+                     v_block_stride, v_token_stride, v_head_stride, out_row_stride,
+                     out_head_stride})
+    fast = fast && (st % vec == 0);
+
+  p.launch_splits = fast ? launch_splits_for(static_cast<int64_t>(page_size) * table_width) : 1;
+  if (p.launch_splits > 1) {
+    const size_t need = rlt_paged_decode_workspace_bytes(num_rows, num_q_heads, head_dim,
+                                                         page_size, table_width);
+    if (workspace == nullptr || workspace_bytes < need || !aligned16(workspace))
+      return RLT_E_WORKSPACE;
+    p.ws_o = static_cast<float*>(workspace);
+    p.ws_ml = p.ws_o + static_cast<size_t>(num_rows) * p.launch_splits * num_q_heads * head_dim;
+  }
+
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  cudaError_t err;
+  switch (dtype) {
+    case RLT_F32: err = launch_typed<float>(p, fast, s); break;
+    case RLT_F16: err = launch_typed<__half>(p, fast, s); break;
+    default: err = launch_typed<__nv_bfloat16>(p, fast, s); break;
+  }
+  return launch_status(err);
+}
