@@ -1,0 +1,423 @@
+"""Benchmark: depth-aware paged decode attention on B200 (HBM GB/s).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+Workload (configs[1] of the reference's hot-path benchmark set): one layer of
+paged decode attention, 256 rows, bf16, 16 query heads = 16 KV heads,
+head_dim 128, page 16, context lengths log-normal (median 2048, sigma 0.6)
+clipped to [128, 8192], LAST-EXITED layout with 4 depth planes (each row
+attends through the table of its own query plane), random page permutation.
+Inputs are seeded synthetic data. One step = one decode call over the batch.
+Each call reads ~5 GB of K/V, far more than the 126 MB L2, so no flush is
+needed between steps.
+
+Multi-GPU (torchrun, one process per GPU): request-sharded replicas with no
+collective on the data path -- every rank runs its own 256-row batch (weak
+scaling); the step time is the max over ranks of the device-timed region.
+
+--impl reference times the reference algorithm's CPU path (the numpy
+restatement in oracle/, the reference being Python) on this box's host cores
+on a bounded sample of the same workload.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+from pathlib import Path
+
+import numpy as np
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+METRIC = "paged decode attn HBM GB/s (% of peak); Ouro-1.4B mixed-depth decode tok/s/GPU"
+WORKLOAD = ("configs[1]: single-layer depth-aware paged decode, 256 rows, bf16, 16x128 heads, "
+            "page 16, ctx lognormal(median 2048, sigma 0.6) in [128, 8192], LAST-EXITED 4 planes")
+FALLBACK_HBM_GBS = 6650.0
+
+
+def parse():
+    p = argparse.ArgumentParser()
+    p.add_argument("--gpus", type=int, default=1)
+    p.add_argument("--steps", type=int, default=20)
+    p.add_argument("--warmup", type=int, default=5)
+    p.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    p.add_argument("--rows", type=int, default=256)
+    p.add_argument("--no-cpu-baseline", action="store_true")
+    return p.parse_args()
+
+
+def measured_peak():
+    path = ROOT / "MEASURED_PEAKS.json"
+    if path.exists():
+        data = json.loads(path.read_text())
+        return float(data["hbm_gbs"]), "measured"
+    return FALLBACK_HBM_GBS, "fallback"
+
+
+def committed_traffic():
+    """Per-launch DRAM bytes of the decode call from the committed ncu summary."""
+    path = ROOT / "profiles" / "decode_config2_traffic.json"
+    if path.exists():
+        return json.loads(path.read_text())
+    return None
+
+
+# ------------------------------------------------------------------ clocks
+
+
+class ClockSampler:
+    """nvidia-smi clocks/throttle sampling during the timed region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index):
+        self.index = index
+        self.proc = None
+        self.file = None
+
+    def __enter__(self):
+        try:
+            self.file = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.FIELDS}",
+                 "--format=csv,noheader,nounits", "-lms", "100"],
+                stdout=self.file, stderr=subprocess.DEVNULL)
+            time.sleep(0.3)
+        except (OSError, FileNotFoundError):
+            self.proc = None
+        return self
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+
+    def summary(self):
+        if self.proc is None or self.file is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.file.flush()
+        rows = []
+        for line in Path(self.file.name).read_text().splitlines():
+            parts = [x.strip() for x in line.split(",")]
+            if len(parts) >= 9 and parts[1].isdigit():
+                rows.append(parts)
+        os.unlink(self.file.name)
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no samples"]}
+        sm = [int(r[1]) for r in rows]
+        loaded = [s for s in sm if s > 300] or sm
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for r in rows for i in range(4) if r[5 + i] == "Active"})
+        return {"sm_mhz": int(statistics.median(loaded)), "sm_max_mhz": int(rows[0][2]),
+                "reasons": reasons, "samples": len(rows)}
+
+
+# --------------------------------------------------------- reference (CPU)
+
+
+def host_sample(plan, rows, seed=0):
+    """Host copy of the selected rows' K/V pages (query plane), compacted."""
+    import oracle
+
+    rng = np.random.default_rng(seed)
+    inputs = []
+    for r in rows:
+        n = int(plan.context_lengths[r])
+        pages = math.ceil(n / plan.page)
+        shape = (pages, plan.page, plan.num_kv_heads, plan.head_dim)
+        k = oracle.f32_to_bf16(rng.standard_normal(shape, dtype=np.float32))
+        v = oracle.f32_to_bf16(rng.standard_normal(shape, dtype=np.float32))
+        q = oracle.f32_to_bf16(rng.standard_normal((1, plan.num_q_heads, plan.head_dim),
+                                                   dtype=np.float32))
+        inputs.append((q, k, v, np.arange(pages, dtype=np.int32)[None], np.array([n])))
+    return inputs
+
+
+def time_cpu(inputs, threads):
+    """Run the oracle over the sample rows on ``threads`` host threads."""
+    import concurrent.futures
+
+    import oracle
+
+    def one(item):
+        q, k, v, t, n = item
+        return oracle.paged_attention(q, k, v, t, n, "bf16")
+
+    start = time.perf_counter()
+    with concurrent.futures.ThreadPoolExecutor(threads) as pool:
+        list(pool.map(one, inputs))
+    return time.perf_counter() - start
+
+
+def cpu_threads():
+    try:
+        from threadpoolctl import threadpool_limits
+
+        threadpool_limits(1)  # one BLAS thread per worker; rows run in parallel
+    except ImportError:
+        pass
+    return os.cpu_count() or 1
+
+
+def sample_rows(plan, target_tokens):
+    order = np.random.default_rng(123).permutation(plan.num_rows)
+    rows, tokens = [], 0
+    for r in order:
+        rows.append(int(r))
+        tokens += int(plan.context_lengths[r])
+        if tokens >= target_tokens:
+            break
+    return rows, tokens
+
+
+def run_reference(args):
+    from vllm_rlt_b200 import workloads
+    from vllm_rlt_b200.kernels.paged_attention import decode_bytes
+
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    plan = workloads.config2_plan(0, rows=args.rows)
+    rows, tokens = sample_rows(plan, 80_000)
+    inputs = host_sample(plan, rows)
+    threads = cpu_threads()
+    step_bytes = decode_bytes([plan.context_lengths[r] for r in rows], 16, 16, 128, 2)
+    for _ in range(args.warmup):
+        time_cpu(inputs, threads)
+    times = [time_cpu(inputs, threads) for _ in range(args.steps)]
+    total = sum(times)
+    value = step_bytes * args.steps / total / 1e9
+    sample = (f"{len(rows)} of {plan.num_rows} rows per step (sum ctx {tokens}), the reference "
+              "algorithm restated in numpy (oracle/), bf16 inputs, fp32 math")
+    line = {
+        "metric": METRIC, "value": round(value, 3), "unit": "GB/s", "impl": "reference",
+        "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": round(total / args.steps * 1e3, 3), "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+        "config": {"workload": WORKLOAD, "sample": sample, "l2": "host run"},
+        "cpu_baseline": {"value": round(value, 3), "unit": "GB/s", "cores": threads,
+                         "kind": "port", "sample": sample},
+        "e2e": {"value": round(value, 3), "unit": "GB/s", "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+# ------------------------------------------------------------------ ours
+
+
+def run_ours(args):
+    import torch
+    import torch.distributed as dist
+
+    import vllm_rlt_b200 as rb
+    from vllm_rlt_b200 import workloads
+    from vllm_rlt_b200.kernels.paged_attention import decode_bytes
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    device = torch.device("cuda", local)
+    if world > 1:
+        import datetime
+
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
+                                device_id=device)
+
+    # Each rank serves its own request shard (seed = rank): weak scaling.
+    plan = workloads.config2_plan(seed=rank, rows=args.rows)
+    g = torch.Generator(device=device).manual_seed(1000 + rank)
+    shape = (plan.num_blocks, 1, plan.page, plan.num_kv_heads, plan.head_dim)
+    key = torch.empty(shape, device=device, dtype=torch.bfloat16)
+    value = torch.empty_like(key)
+    for t in (key, value):  # fill in chunks to bound the fp32 temporary
+        flat = t.view(-1)
+        step = 1 << 28
+        for s in range(0, flat.numel(), step):
+            n = min(step, flat.numel() - s)
+            flat[s : s + n].copy_(torch.randn(n, generator=g, device=device))
+    k_layer, v_layer = key[:, 0], value[:, 0]
+    tables_np = plan.block_tables()
+    tables = torch.from_numpy(tables_np).to(device)
+    lengths = torch.from_numpy(plan.context_lengths).to(device)
+    q = torch.randn((plan.num_rows, 16, 128), generator=g, device=device).to(torch.bfloat16)
+    backend = rb.B200PagedAttention(device, torch.bfloat16, 128, plan.page)
+    step_bytes = decode_bytes(plan.context_lengths, 16, 16, 128, 2, plan.page)
+    splits_needed = bool((plan.context_lengths > 256).any())
+    launches_per_step = 2 if splits_needed else 1
+
+    stream = torch.cuda.current_stream(device)
+
+    def barrier():
+        if world > 1:
+            dist.barrier(device_ids=[local])
+
+    # ---- device-resident timing (value) + per-launch events (roofline)
+    for _ in range(args.warmup):
+        backend(q, k_layer, v_layer, tables, lengths)
+    torch.cuda.synchronize(device)
+    starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    t0 = torch.cuda.Event(enable_timing=True)
+    t1 = torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clocks:
+        barrier()
+        torch.cuda.synchronize(device)
+        t0.record(stream)
+        for i in range(args.steps):
+            starts[i].record(stream)
+            out = backend(q, k_layer, v_layer, tables, lengths)
+            ends[i].record(stream)
+        t1.record(stream)
+        torch.cuda.synchronize(device)
+        barrier()
+    elapsed_ms = t0.elapsed_time(t1)
+    launch_ms = [s.elapsed_time(e) for s, e in zip(starts, ends)]
+    errors = backend.check_errors()
+    if errors:
+        raise RuntimeError(f"kernel reported metadata errors: {errors}")
+
+    # ---- end to end through the public API with host buffers
+    pin = dict(
+        q=q.cpu().pin_memory(), tables=tables.cpu().pin_memory(),
+        lengths=lengths.cpu().pin_memory(),
+    )
+    out_host = torch.empty(out.shape, dtype=out.dtype, pin_memory=True)
+    h2d = sum(t.numel() * t.element_size() for t in pin.values())
+    d2h = out_host.numel() * out_host.element_size()
+
+    def e2e_step():
+        qd = pin["q"].to(device, non_blocking=True)
+        td = pin["tables"].to(device, non_blocking=True)
+        ld = pin["lengths"].to(device, non_blocking=True)
+        o = backend(qd, k_layer, v_layer, td, ld)
+        out_host.copy_(o, non_blocking=True)
+
+    for _ in range(args.warmup):
+        e2e_step()
+    torch.cuda.synchronize(device)
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    barrier()
+    torch.cuda.synchronize(device)
+    e0.record(stream)
+    for _ in range(args.steps):
+        e2e_step()
+    e1.record(stream)
+    torch.cuda.synchronize(device)
+    barrier()
+    e2e_ms = e0.elapsed_time(e1)
+
+    # ---- max over ranks; bytes summed over ranks
+    stats = torch.tensor([elapsed_ms, e2e_ms, float(step_bytes)], dtype=torch.float64,
+                         device=device)
+    if world > 1:
+        worst = stats[:2].clone()
+        dist.all_reduce(worst, op=dist.ReduceOp.MAX)
+        total_bytes = stats[2:].clone()
+        dist.all_reduce(total_bytes, op=dist.ReduceOp.SUM)
+        elapsed_ms, e2e_ms = worst.tolist()
+        job_bytes = total_bytes.item()
+    else:
+        job_bytes = float(step_bytes)
+    value = job_bytes * args.steps / (elapsed_ms / 1e3) / 1e9
+    e2e_value = job_bytes * args.steps / (e2e_ms / 1e3) / 1e9
+    peak, peak_kind = measured_peak()
+    kernel_ms = statistics.mean(launch_ms)
+    achieved = step_bytes / (kernel_ms / 1e3) / 1e9
+    traffic = committed_traffic()
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        rows, tokens = sample_rows(plan, 80_000)
+        inputs = host_sample(plan, rows)
+        threads = cpu_threads()
+        sample_bytes = decode_bytes([plan.context_lengths[r] for r in rows], 16, 16, 128, 2)
+        time_cpu(inputs[:2], threads)
+        reps, spent = 0, 0.0
+        while spent < 10.0 and reps < 50:
+            spent += time_cpu(inputs, threads)
+            reps += 1
+        cpu = {
+            "value": round(sample_bytes * reps / spent / 1e9, 3), "unit": "GB/s",
+            "cores": threads, "kind": "port",
+            "sample": (f"{len(rows)} of {plan.num_rows} rows (sum ctx {tokens}) x {reps} reps, "
+                       "numpy restatement of the reference's torch path, fp32 math"),
+        }
+
+    if world > 1:
+        dist.barrier(device_ids=[local])
+        dist.destroy_process_group()
+    if rank != 0:
+        return
+    line = {
+        "metric": METRIC,
+        "value": round(value, 2),
+        "unit": "GB/s",
+        "n_gpus": world,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": round(elapsed_ms / args.steps, 4),
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": "bf16",
+        "data": "synthetic",
+        "pct_of_peak": round(100.0 * value / world / peak, 2),
+        "config": {
+            "workload": WORKLOAD,
+            "rows_per_gpu": plan.num_rows,
+            "sum_ctx_per_gpu": int(plan.context_lengths.sum()),
+            "bytes_per_step_per_gpu": int(step_bytes),
+            "l2": "no flush: each step reads ~5 GB of K/V (> 126 MB L2)",
+            "parallelism": f"{world} request-sharded replicas, no data-path collective",
+        },
+        "roofline": {
+            "bound": "hbm",
+            "achieved": round(achieved, 1),
+            "peak": peak,
+            "unit": "GB/s",
+            "frac": round(achieved / peak, 4),
+            "peak_kind": peak_kind,
+            "kernel": "decode call (split decode kernel + split combine), CUDA events per launch",
+            "traffic": None if traffic is None else traffic.get("bytes_per_launch"),
+        },
+        "e2e": {
+            "value": round(e2e_value, 2),
+            "unit": "GB/s",
+            "h2d_bytes_per_step": int(h2d),
+            "d2h_bytes_per_step": int(d2h),
+        },
+        "gpu_launches": launches_per_step * args.steps,
+        "clocks": clocks.summary(),
+    }
+    if cpu is not None:
+        line["cpu_baseline"] = cpu
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    args = parse()
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_ours(args)
+
+
+if __name__ == "__main__":
+    main()

@@ -86,6 +86,33 @@ int rlt_paged_decode(const void* q, const void* key_cache, const void* value_cac
                      int64_t table_row_stride, int64_t out_row_stride, int64_t out_head_stride,
                      float scale, void* stream);
 
+/* Bytes of scratch rlt_paged_prefill needs: per-token (table row, causal
+ * length) pairs plus the split-KV partials of the CUDA-core path. */
+size_t rlt_paged_prefill_workspace_bytes(int32_t num_tokens, int32_t num_q_heads,
+                                         int32_t head_dim, int32_t page_size,
+                                         int32_t table_width);
+
+/* Packed chunked-prefill paged causal attention with bottom-right alignment:
+ * sequence s owns query tokens cu_seqlens_q[s] .. cu_seqlens_q[s+1]-1 and
+ * keys 0 .. context_lengths[s]-1 through block_tables[s]; query i of the
+ * chunk (0-based) sees keys up to context_lengths[s] - qlen_s + i.
+ * The chunk's own K/V are already written to the pool (no gathering).
+ * max_seqlen_q is accepted for interface parity and never shapes a launch.
+ * Replaces: vllm_rlt/kernels/flash_attention.py:66-96
+ * (FlashPagedAttention.prefill, FA4 flash_attn_varlen_func with page_table,
+ * seqused_k, causal=True), called from vllm_rlt/core/kv_cache_manager.py:570-579. */
+int rlt_paged_prefill(const void* q, const void* key_cache, const void* value_cache,
+                      const int32_t* block_tables, const int32_t* context_lengths,
+                      const int32_t* cu_seqlens_q, void* out, void* workspace,
+                      size_t workspace_bytes, int32_t* status, int32_t dtype, int32_t num_tokens,
+                      int32_t num_seqs, int32_t max_seqlen_q, int32_t num_q_heads,
+                      int32_t num_kv_heads, int32_t head_dim, int32_t page_size,
+                      int32_t table_width, int64_t num_blocks, int64_t q_row_stride,
+                      int64_t q_head_stride, int64_t k_block_stride, int64_t k_token_stride,
+                      int64_t k_head_stride, int64_t v_block_stride, int64_t v_token_stride,
+                      int64_t v_head_stride, int64_t table_row_stride, int64_t out_row_stride,
+                      int64_t out_head_stride, float scale, void* stream);
+
 /* KV page write into the depth plane (reshape_and_cache):
  *   key_cache[write_blocks[i], layer, write_offsets[i]] = k[i]   (i < num_rows)
  *   value_cache[...]                                    = v[i]

@@ -1,0 +1,86 @@
+"""Packed chunked prefill on the B200 vs the reference (golden vectors)."""
+
+from __future__ import annotations
+
+import math
+
+import numpy as np
+import pytest
+import torch
+
+import oracle
+import vllm_rlt_b200 as rb
+from gpu_helpers import TORCH, CudaWriter, to_numpy, to_torch
+from helpers import assert_close, digest, load
+
+pytestmark = pytest.mark.gpu
+
+
+def rebuild(dtype):
+    fx = load(f"prefill_{dtype}")
+    writer = CudaWriter((80, 2, 16, 2, 64), dtype)
+    rng = np.random.default_rng(fx["prefix_seed"].tolist())
+    for rid, depth, prefix, count in fx["spec"].tolist():
+        for layer in range(2):
+            if prefix:
+                kv = oracle.from_f32(rng.standard_normal((prefix, 2, 64), dtype=np.float32), dtype)
+                neg = oracle.from_f32(-oracle.to_f32(kv, dtype), dtype)
+                for p in range(prefix):
+                    writer.write(layer, int(fx["alloc_tables"][rid, depth, p // 16]), p % 16,
+                                 kv[p], neg[p])
+    writer.flush()
+    return fx, writer
+
+
+@pytest.mark.parametrize("dtype", ["f32", "f16", "bf16"])
+def test_packed_prefill_matches_reference(dtype):
+    fx, writer = rebuild(dtype)
+    blocks = torch.from_numpy(fx["write_blocks"]).cuda()
+    offsets = torch.from_numpy(fx["write_offsets"]).cuda()
+    backend = rb.B200PagedAttention("cuda", TORCH[dtype], 64, 16)
+    for layer in range(2):
+        rb.write_kv(writer.key, writer.value, layer, blocks, offsets,
+                    to_torch(fx[f"k{layer}"], dtype), to_torch(fx[f"v{layer}"], dtype))
+        out = backend.prefill(to_torch(fx[f"q{layer}"], dtype), writer.key[:, layer],
+                              writer.value[:, layer], torch.from_numpy(fx["block_tables"]).cuda(),
+                              torch.from_numpy(fx["context_lengths"]).cuda(),
+                              torch.from_numpy(fx["cu_seqlens_q"]).cuda(), int(fx["max_seqlen_q"]))
+        torch.cuda.synchronize()
+        assert_close(to_numpy(out), fx[f"out{layer}"], dtype)
+    key, value = writer.numpy()
+    assert digest(key) == str(fx["key_digest"])
+    assert digest(value) == str(fx["value_digest"])
+    assert backend.check_errors() == []
+
+
+@pytest.mark.parametrize("dtype", ["bf16", "f16"])
+def test_chunked_prefill_with_prefix_reuse_vs_oracle(dtype):
+    """Config-4-shaped (scaled down): several sequences, chunk after a reused
+    prefix, fragmented tables, GQA 1, head_dim 128."""
+    rng = np.random.default_rng(7)
+    page, hkv, d = 16, 4, 128
+    prompt = [300, 517, 64, 1000]
+    prefix = [0, 256, 17, 640]
+    chunk = [min(200, p - s) for p, s in zip(prompt, prefix)]
+    lengths = [s + c for s, c in zip(prefix, chunk)]
+    width = max(math.ceil(n / page) for n in lengths)
+    num_blocks = sum(math.ceil(n / page) for n in lengths) + 3
+    perm = rng.permutation(num_blocks)
+    tables = np.full((len(lengths), width), -1, dtype=np.int32)
+    c = 0
+    for i, n in enumerate(lengths):
+        pages = math.ceil(n / page)
+        tables[i, :pages] = perm[c : c + pages]
+        c += pages
+    g = torch.Generator(device="cuda").manual_seed(5)
+    td = TORCH[dtype]
+    key = torch.randn(num_blocks, 1, page, hkv, d, generator=g, device="cuda").to(td)
+    value = torch.randn(num_blocks, 1, page, hkv, d, generator=g, device="cuda").to(td)
+    cu = np.concatenate([[0], np.cumsum(chunk)]).astype(np.int32)
+    q = torch.randn(int(cu[-1]), hkv, d, generator=g, device="cuda").to(td)
+    out = rb.paged_prefill(q, key[:, 0], value[:, 0], torch.from_numpy(tables).cuda(),
+                           torch.tensor(lengths, dtype=torch.int32, device="cuda"),
+                           torch.from_numpy(cu).cuda(), max(chunk))
+    expected = oracle.paged_prefill(to_numpy(q), to_numpy(key[:, 0]), to_numpy(value[:, 0]),
+                                    tables, np.array(lengths), cu, dtype)
+    assert_close(to_numpy(out), expected, dtype)

@@ -39,6 +39,7 @@ struct DecodeParams {
   const void* v;
   const int32_t* tables;
   const int32_t* lengths;
+  const int32_t* table_index;  // optional row -> table row map (packed prefill); NULL = identity
   void* out;
   float* ws_o;   // [rows, launch_splits, hq, head_dim] unnormalised acc
   float* ws_ml;  // [rows, launch_splits, hq, 2] (running max in log2 units, sum)
@@ -165,7 +166,7 @@ __global__ void __launch_bounds__(kDecodeWarps * 32, 4)
 
   const T* kbase = static_cast<const T*>(p.k) + kvh * p.k_hs + s * VEC;
   const T* vbase = static_cast<const T*>(p.v) + kvh * p.v_hs + s * VEC;
-  const int32_t* trow = p.tables + row * p.t_rs;
+  const int32_t* trow = p.tables + (p.table_index ? p.table_index[row] : row) * p.t_rs;
   const int tl = s >> PLAIN;  // token (within the group) whose score this lane ends with
   const bool writer = (s & ((1 << PLAIN) - 1)) == 0;
   const uint4 zero4 = make_uint4(0, 0, 0, 0);
@@ -408,7 +409,7 @@ __global__ void __launch_bounds__(128) paged_decode_generic_kernel(const __grid_
     acc[i] = 0.f;
   }
   float m = -INFINITY, l = 0.f;
-  const int32_t* trow = p.tables + row * p.t_rs;
+  const int32_t* trow = p.tables + (p.table_index ? p.table_index[row] : row) * p.t_rs;
   for (int t = 0; t < ctx; ++t) {
     const int blk = __ldg(trow + t / p.page);
     if (blk < 0 || blk >= p.num_blocks) {
@@ -443,6 +444,32 @@ __global__ void __launch_bounds__(128) paged_decode_generic_kernel(const __grid_
     const int d = lane + 32 * i;
     if (d < D) op[d] = from_f32<T>(acc[i] * inv);
   }
+}
+
+// Packed chunked prefill as decode rows (vllm_rlt/kernels/flash_attention.py:
+// 66-96 semantics): token i of sequence s (cu[s] <= i < cu[s+1]) reads table
+// row s with the bottom-right causal length len_s - qlen_s + (i - cu[s]) + 1.
+__global__ void prefill_rows_kernel(const int32_t* __restrict__ cu, const int32_t* __restrict__ lengths,
+                                    int32_t* __restrict__ row_seq, int32_t* __restrict__ row_len,
+                                    int32_t* status, int num_tokens, int num_seqs) {
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= num_tokens) return;
+  // last s with cu[s] <= i
+  int lo = 0, hi = num_seqs - 1;
+  while (lo < hi) {
+    const int mid = (lo + hi + 1) >> 1;
+    if (cu[mid] <= i) lo = mid; else hi = mid - 1;
+  }
+  const int begin = cu[lo], stop = cu[lo + 1];
+  if (i < begin || i >= stop) {
+    raise_status(status, kStatusBadSequence);
+    row_seq[i] = 0;
+    row_len[i] = 0;
+    return;
+  }
+  const int len = lengths[lo] - (stop - begin) + (i - begin) + 1;
+  row_seq[i] = lo;
+  row_len[i] = len > 0 ? len : 0;
 }
 
 template <typename T, int D, int GC>
@@ -512,13 +539,99 @@ using namespace rlt;
 
 extern "C" int rlt_version(void) { return 100; }
 
+namespace {
+
+struct DecodeArgs {
+  const void* q;
+  const void* k;
+  const void* v;
+  const int32_t* tables;
+  int32_t* status;
+  int32_t dtype, rows, hq, hkv, head_dim, page, width;
+  int64_t num_blocks, q_rs, q_hs, k_bs, k_ts, k_hs, v_bs, v_ts, v_hs, t_rs, o_rs, o_hs;
+  void* out;
+  float scale;
+};
+
+size_t split_bytes(int rows, int hq, int head_dim, int page, int width) {
+  const int splits = launch_splits_for(static_cast<int64_t>(page) * width);
+  if (splits <= 1 || rows <= 0 || hq <= 0 || head_dim <= 0) return 0;
+  return static_cast<size_t>(rows) * splits * hq * (head_dim + 2) * sizeof(float);
+}
+
+size_t align16(size_t n) { return (n + 15) & ~static_cast<size_t>(15); }
+
+int validate(const DecodeArgs& a) {
+  if (elem_size(a.dtype) == 0) return RLT_E_DTYPE;
+  if (a.head_dim <= 0 || a.head_dim > 256) return RLT_E_HEAD_DIM;
+  if (a.hq <= 0 || a.hkv <= 0 || a.hq % a.hkv) return RLT_E_HEADS;
+  if (a.rows < 0 || a.page <= 0 || a.width < 0 || a.num_blocks < 0) return RLT_E_SHAPE;
+  return RLT_OK;
+}
+
+// Fill the kernel parameters and pick the vector or generic kernel.
+DecodeParams make_params(const DecodeArgs& a, bool* fast) {
+  DecodeParams p{};
+  p.q = a.q;
+  p.k = a.k;
+  p.v = a.v;
+  p.tables = a.tables;
+  p.out = a.out;
+  p.status = a.status;
+  p.rows = a.rows;
+  p.hq = a.hq;
+  p.hkv = a.hkv;
+  p.group = a.hq / a.hkv;
+  p.head_dim = a.head_dim;
+  p.page = a.page;
+  p.width = a.width;
+  p.num_blocks = a.num_blocks;
+  p.q_rs = a.q_rs;
+  p.q_hs = a.q_hs;
+  p.k_bs = a.k_bs;
+  p.k_ts = a.k_ts;
+  p.k_hs = a.k_hs;
+  p.v_bs = a.v_bs;
+  p.v_ts = a.v_ts;
+  p.v_hs = a.v_hs;
+  p.t_rs = a.t_rs;
+  p.o_rs = a.o_rs;
+  p.o_hs = a.o_hs;
+  p.scale_log2 = a.scale * 1.4426950408889634f;
+  // The 16-byte vector contract: every base pointer and every stride that
+  // moves between head rows is a multiple of 16 bytes.
+  const int esize = elem_size(a.dtype);
+  const int64_t vec = 16 / esize;
+  bool ok = fast_head_dim(a.head_dim, esize) && aligned16(a.q) && aligned16(a.k) &&
+            aligned16(a.v) && aligned16(a.out);
+  for (int64_t st : {a.q_rs, a.q_hs, a.k_bs, a.k_ts, a.k_hs, a.v_bs, a.v_ts, a.v_hs, a.o_rs,
+                     a.o_hs})
+    ok = ok && (st % vec == 0);
+  *fast = ok;
+  p.launch_splits = ok ? launch_splits_for(static_cast<int64_t>(a.page) * a.width) : 1;
+  return p;
+}
+
+int run(DecodeParams p, int32_t dtype, bool fast, void* split_ws, cudaStream_t s) {
+  if (p.launch_splits > 1) {
+    p.ws_o = static_cast<float*>(split_ws);
+    p.ws_ml = p.ws_o + static_cast<size_t>(p.rows) * p.launch_splits * p.hq * p.head_dim;
+  }
+  cudaError_t err;
+  switch (dtype) {
+    case RLT_F32: err = launch_typed<float>(p, fast, s); break;
+    case RLT_F16: err = launch_typed<__half>(p, fast, s); break;
+    default: err = launch_typed<__nv_bfloat16>(p, fast, s); break;
+  }
+  return launch_status(err);
+}
+
+}  // namespace
+
 extern "C" size_t rlt_paged_decode_workspace_bytes(int32_t num_rows, int32_t num_q_heads,
                                                    int32_t head_dim, int32_t page_size,
                                                    int32_t table_width) {
-  if (num_rows <= 0 || num_q_heads <= 0 || head_dim <= 0) return 0;
-  const int splits = launch_splits_for(static_cast<int64_t>(page_size) * table_width);
-  if (splits <= 1) return 0;
-  return static_cast<size_t>(num_rows) * splits * num_q_heads * (head_dim + 2) * sizeof(float);
+  return split_bytes(num_rows, num_q_heads, head_dim, page_size, table_width);
 }
 
 extern "C" int rlt_paged_decode(const void* q, const void* key_cache, const void* value_cache,
@@ -533,68 +646,73 @@ extern "C" int rlt_paged_decode(const void* q, const void* key_cache, const void
                                 int64_t v_token_stride, int64_t v_head_stride,
                                 int64_t table_row_stride, int64_t out_row_stride,
                                 int64_t out_head_stride, float scale, void* stream) {
-  const int esize = elem_size(dtype);
-  if (esize == 0) return RLT_E_DTYPE;
-  if (head_dim <= 0 || head_dim > 256) return RLT_E_HEAD_DIM;
-  if (num_q_heads <= 0 || num_kv_heads <= 0 || num_q_heads % num_kv_heads) return RLT_E_HEADS;
-  if (num_rows < 0 || page_size <= 0 || table_width < 0 || num_blocks < 0) return RLT_E_SHAPE;
+  const DecodeArgs a{q, key_cache, value_cache, block_tables, status, dtype, num_rows,
+                     num_q_heads, num_kv_heads, head_dim, page_size, table_width, num_blocks,
+                     q_row_stride, q_head_stride, k_block_stride, k_token_stride, k_head_stride,
+                     v_block_stride, v_token_stride, v_head_stride, table_row_stride,
+                     out_row_stride, out_head_stride, out, scale};
+  const int bad = validate(a);
+  if (bad != RLT_OK) return bad;
   if (num_rows == 0) return RLT_OK;
-
-  DecodeParams p{};
-  p.q = q;
-  p.k = key_cache;
-  p.v = value_cache;
-  p.tables = block_tables;
+  bool fast = false;
+  DecodeParams p = make_params(a, &fast);
   p.lengths = context_lengths;
-  p.out = out;
-  p.status = status;
-  p.rows = num_rows;
-  p.hq = num_q_heads;
-  p.hkv = num_kv_heads;
-  p.group = num_q_heads / num_kv_heads;
-  p.head_dim = head_dim;
-  p.page = page_size;
-  p.width = table_width;
-  p.num_blocks = num_blocks;
-  p.q_rs = q_row_stride;
-  p.q_hs = q_head_stride;
-  p.k_bs = k_block_stride;
-  p.k_ts = k_token_stride;
-  p.k_hs = k_head_stride;
-  p.v_bs = v_block_stride;
-  p.v_ts = v_token_stride;
-  p.v_hs = v_head_stride;
-  p.t_rs = table_row_stride;
-  p.o_rs = out_row_stride;
-  p.o_hs = out_head_stride;
-  p.scale_log2 = scale * 1.4426950408889634f;
-
-  // The 16-byte vector contract: every base pointer and every stride that
-  // moves between head rows is a multiple of 16 bytes.
-  const int64_t vec = 16 / esize;
-  bool fast = fast_head_dim(head_dim, esize) && aligned16(q) && aligned16(key_cache) &&
-              aligned16(value_cache) && aligned16(out);
-  for (int64_t st : {q_row_stride, q_head_stride, k_block_stride, k_token_stride, k_head_stride,
-                     v_block_stride, v_token_stride, v_head_stride, out_row_stride,
-                     out_head_stride})
-    fast = fast && (st % vec == 0);
-
-  p.launch_splits = fast ? launch_splits_for(static_cast<int64_t>(page_size) * table_width) : 1;
   if (p.launch_splits > 1) {
-    const size_t need = rlt_paged_decode_workspace_bytes(num_rows, num_q_heads, head_dim,
-                                                         page_size, table_width);
+    const size_t need = split_bytes(num_rows, num_q_heads, head_dim, page_size, table_width);
     if (workspace == nullptr || workspace_bytes < need || !aligned16(workspace))
       return RLT_E_WORKSPACE;
-    p.ws_o = static_cast<float*>(workspace);
-    p.ws_ml = p.ws_o + static_cast<size_t>(num_rows) * p.launch_splits * num_q_heads * head_dim;
   }
+  return run(p, dtype, fast, workspace, static_cast<cudaStream_t>(stream));
+}
 
+extern "C" size_t rlt_paged_prefill_workspace_bytes(int32_t num_tokens, int32_t num_q_heads,
+                                                    int32_t head_dim, int32_t page_size,
+                                                    int32_t table_width) {
+  if (num_tokens <= 0) return 0;
+  return align16(static_cast<size_t>(num_tokens) * 2 * sizeof(int32_t)) +
+         split_bytes(num_tokens, num_q_heads, head_dim, page_size, table_width);
+}
+
+extern "C" int rlt_paged_prefill(const void* q, const void* key_cache, const void* value_cache,
+                                 const int32_t* block_tables, const int32_t* context_lengths,
+                                 const int32_t* cu_seqlens_q, void* out, void* workspace,
+                                 size_t workspace_bytes, int32_t* status, int32_t dtype,
+                                 int32_t num_tokens, int32_t num_seqs, int32_t max_seqlen_q,
+                                 int32_t num_q_heads, int32_t num_kv_heads, int32_t head_dim,
+                                 int32_t page_size, int32_t table_width, int64_t num_blocks,
+                                 int64_t q_row_stride, int64_t q_head_stride,
+                                 int64_t k_block_stride, int64_t k_token_stride,
+                                 int64_t k_head_stride, int64_t v_block_stride,
+                                 int64_t v_token_stride, int64_t v_head_stride,
+                                 int64_t table_row_stride, int64_t out_row_stride,
+                                 int64_t out_head_stride, float scale, void* stream) {
+  (void)max_seqlen_q;  // the launch shape never depends on host-known lengths
+  const DecodeArgs a{q, key_cache, value_cache, block_tables, status, dtype, num_tokens,
+                     num_q_heads, num_kv_heads, head_dim, page_size, table_width, num_blocks,
+                     q_row_stride, q_head_stride, k_block_stride, k_token_stride, k_head_stride,
+                     v_block_stride, v_token_stride, v_head_stride, table_row_stride,
+                     out_row_stride, out_head_stride, out, scale};
+  const int bad = validate(a);
+  if (bad != RLT_OK) return bad;
+  if (num_seqs < 0) return RLT_E_SHAPE;
+  if (num_tokens == 0) return RLT_OK;
+  if (num_seqs == 0) return RLT_E_SHAPE;
+  const size_t need = rlt_paged_prefill_workspace_bytes(num_tokens, num_q_heads, head_dim,
+                                                        page_size, table_width);
+  if (workspace == nullptr || workspace_bytes < need || !aligned16(workspace))
+    return RLT_E_WORKSPACE;
+  int32_t* row_seq = static_cast<int32_t*>(workspace);
+  int32_t* row_len = row_seq + num_tokens;
+  void* split_ws =
+      static_cast<char*>(workspace) + align16(static_cast<size_t>(num_tokens) * 2 * sizeof(int32_t));
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  cudaError_t err;
-  switch (dtype) {
-    case RLT_F32: err = launch_typed<float>(p, fast, s); break;
-    case RLT_F16: err = launch_typed<__half>(p, fast, s); break;
-    default: err = launch_typed<__nv_bfloat16>(p, fast, s); break;
-  }
-  return launch_status(err);
+  prefill_rows_kernel<<<ceil_div(num_tokens, 256), 256, 0, s>>>(
+      cu_seqlens_q, context_lengths, row_seq, row_len, status, num_tokens, num_seqs);
+  cudaError_t err = cudaGetLastError();
+  if (err != cudaSuccess) return launch_status(err);
+  bool fast = false;
+  DecodeParams p = make_params(a, &fast);
+  p.lengths = row_len;
+  p.table_index = row_seq;
+  return run(p, dtype, fast, split_ws, s);
 }
