@@ -48,6 +48,7 @@ extern "C" {
 #define RLT_E_SHAPE -5
 #define RLT_E_ALIGN -6
 #define RLT_E_DEVICE -7
+#define RLT_E_SCRATCH -8
 
 /* status bits */
 #define RLT_STATUS_BAD_LENGTH 1
@@ -112,6 +113,39 @@ int rlt_paged_prefill(const void* q, const void* key_cache, const void* value_ca
                       int64_t k_head_stride, int64_t v_block_stride, int64_t v_token_stride,
                       int64_t v_head_stride, int64_t table_row_stride, int64_t out_row_stride,
                       int64_t out_head_stride, float scale, void* stream);
+
+/* Size of the static split-KV scratch of rlt_paged_decode_noalloc (bytes). */
+#define RLT_NOALLOC_SCRATCH_BYTES (16u << 20)
+
+/* rlt_paged_decode for callers that cannot allocate device memory when they
+ * run attention (a runtime that reserves all device memory for its own pool,
+ * a host that forbids driver allocations after start-up, or code where an
+ * allocation would synchronise the device). Same inputs, outputs and results
+ * as rlt_paged_decode; there is no workspace argument: the split-KV scratch is
+ * a 16 MiB (RLT_NOALLOC_SCRATCH_BYTES) device array inside the library that
+ * every GPU using this entry point holds until the process exits. It calls no
+ * cudaMalloc/cudaFree or other allocating routine.
+ *  - The first call on a device looks up that device's copy of the array
+ *    (with the device current); make that first call before any stream
+ *    capture on the device.
+ *  - Returns RLT_E_SCRATCH, launching nothing, when the launch shape needs
+ *    more than the array holds: rlt_paged_decode_workspace_bytes(num_rows,
+ *    num_q_heads, head_dim, page_size, table_width) > RLT_NOALLOC_SCRATCH_BYTES.
+ *  - All calls share the array; calls that overlap on the GPU race on it, so
+ *    serialise them (one stream, or events between streams).
+ * This entry point has no counterpart in the reference, which always
+ * allocates its outputs and scratch through torch. */
+int rlt_paged_decode_noalloc(const void* q, const void* key_cache, const void* value_cache,
+                             const int32_t* block_tables, const int32_t* context_lengths,
+                             void* out, int32_t* status, int32_t dtype, int32_t num_rows,
+                             int32_t num_q_heads, int32_t num_kv_heads, int32_t head_dim,
+                             int32_t page_size, int32_t table_width, int64_t num_blocks,
+                             int64_t q_row_stride, int64_t q_head_stride, int64_t k_block_stride,
+                             int64_t k_token_stride, int64_t k_head_stride,
+                             int64_t v_block_stride, int64_t v_token_stride,
+                             int64_t v_head_stride, int64_t table_row_stride,
+                             int64_t out_row_stride, int64_t out_head_stride, float scale,
+                             void* stream);
 
 /* KV page write into the depth plane (reshape_and_cache):
  *   key_cache[write_blocks[i], layer, write_offsets[i]] = k[i]   (i < num_rows)

@@ -28,6 +28,7 @@ ERRORS = {
     -5: "invalid shape",
     -6: "misaligned pointer",
     -7: "no suitable CUDA device",
+    -8: "launch shape needs more split scratch than the library's static array holds",
 }
 
 STATUS_BITS = {
@@ -57,6 +58,7 @@ SIGNATURES = {
         + [_i64] * 12
         + [_f32, _p],
     ),
+    "rlt_paged_decode_noalloc": (_i32, [_p] * 7 + [_i32] * 7 + [_i64] * 12 + [_f32, _p]),
     "rlt_paged_prefill_workspace_bytes": (_sz, [_i32, _i32, _i32, _i32, _i32]),
     "rlt_paged_prefill": (
         _i32,

@@ -628,6 +628,40 @@ int run(DecodeParams p, int32_t dtype, bool fast, void* split_ws, cudaStream_t s
 
 }  // namespace
 
+namespace rlt {
+namespace detail {
+
+// Decode with caller-provided split scratch of `capacity` bytes (the static
+// scratch of the no-allocation entry point). Same kernels, same split plan
+// and therefore the same results as rlt_paged_decode.
+int paged_decode_into(const void* q, const void* key_cache, const void* value_cache,
+                      const int32_t* block_tables, const int32_t* context_lengths, void* out,
+                      void* scratch, size_t capacity, int32_t* status, int32_t dtype,
+                      int32_t num_rows, int32_t num_q_heads, int32_t num_kv_heads,
+                      int32_t head_dim, int32_t page_size, int32_t table_width,
+                      int64_t num_blocks, const int64_t* strides, float scale,
+                      cudaStream_t stream, size_t* needed) {
+  const DecodeArgs a{q, key_cache, value_cache, block_tables, status, dtype, num_rows,
+                     num_q_heads, num_kv_heads, head_dim, page_size, table_width, num_blocks,
+                     strides[0], strides[1], strides[2], strides[3], strides[4], strides[5],
+                     strides[6], strides[7], strides[8], strides[9], strides[10], out, scale};
+  const int bad = validate(a);
+  if (bad != RLT_OK) return bad;
+  if (num_rows == 0) return RLT_OK;
+  bool fast = false;
+  DecodeParams p = make_params(a, &fast);
+  p.lengths = context_lengths;
+  *needed = 0;
+  if (p.launch_splits > 1) {
+    *needed = split_bytes(num_rows, num_q_heads, head_dim, page_size, table_width);
+    if (*needed > capacity) return RLT_E_WORKSPACE;
+  }
+  return run(p, dtype, fast, scratch, stream);
+}
+
+}  // namespace detail
+}  // namespace rlt
+
 extern "C" size_t rlt_paged_decode_workspace_bytes(int32_t num_rows, int32_t num_q_heads,
                                                    int32_t head_dim, int32_t page_size,
                                                    int32_t table_width) {
