@@ -56,6 +56,7 @@ extern "C" {
 #define RLT_STATUS_BAD_OFFSET 4
 #define RLT_STATUS_BAD_SLOT 8
 #define RLT_STATUS_BAD_SEQUENCE 16
+#define RLT_STATUS_TIMEOUT 32 /* a bounded wait inside a tensor-core kernel gave up */
 
 /* Library version (major*10000 + minor*100 + patch). */
 int rlt_version(void);
@@ -113,6 +114,13 @@ int rlt_paged_prefill(const void* q, const void* key_cache, const void* value_ca
                       int64_t k_head_stride, int64_t v_block_stride, int64_t v_token_stride,
                       int64_t v_head_stride, int64_t table_row_stride, int64_t out_row_stride,
                       int64_t out_head_stride, float scale, void* stream);
+
+/* 1 if rlt_paged_prefill runs this dtype/head_dim/page on the tcgen05
+ * tensor-core kernel (bf16/fp16, head_dim 128, page in {8..128}; all
+ * pointers and strides 16-byte aligned), 0 if on the CUDA-core path (fp32,
+ * other head_dims or pages). No counterpart in the reference, whose FA4
+ * wheel makes the same choice internally. */
+int rlt_paged_prefill_uses_tensor_cores(int32_t dtype, int32_t head_dim, int32_t page_size);
 
 /* Size of the static split-KV scratch of rlt_paged_decode_noalloc (bytes). */
 #define RLT_NOALLOC_SCRATCH_BYTES (16u << 20)

@@ -208,7 +208,7 @@ def make_shared(dtype):
              dtype=dtype, layout="shared", ops=ops, queries=queries, seed=5)
 
 
-def make_prefill(dtype):
+def make_prefill(dtype, d=64, spec=None, max_tokens=65, blocks=80, tag="", store_inputs=True):
     """Packed chunked prefill with prefixes at unequal depths crossing page
     boundaries (reference tests/test_flash_attention.py:146-189): the packed
     batch's metadata from _prepare_batch(packed_prefill=True) and the expected
@@ -219,20 +219,20 @@ def make_prefill(dtype):
     from vllm_rlt.kernels.paged_attention import torch_paged_attention
 
     td = TORCH_DTYPES[dtype]
-    cache = KVCacheManager(2, 2, 64, 80, 16, 4, "cpu", td, "torch")
+    cache = KVCacheManager(2, 2, d, blocks, 16, 4, "cpu", td, "torch")
     cache.attention = SimpleNamespace(generation=4)
     cache.key_cache.zero_()
     cache.value_cache.zero_()
     rng = np.random.default_rng([712, 2])
     for rid in ["hole", "a", "b", "c"]:
-        cache.allocate(rid, 65)
+        cache.allocate(rid, max_tokens)
     cache.free("hole")
     ids, depths, positions = [], [], []
-    spec = [("a", 0, 0, 19), ("b", 2, 17, 7), ("c", 3, 31, 18)]
+    spec = spec or [("a", 0, 0, 19), ("b", 2, 17, 7), ("c", 3, 31, 18)]
     for rid, depth, prefix, count in spec:
         for layer in range(2):
             if prefix:
-                kv = values(rng, (prefix, 2, 64), dtype)
+                kv = values(rng, (prefix, 2, d), dtype)
                 cache.write(layer, [rid] * prefix, [depth] * prefix, list(range(prefix)), kv, -kv)
         ids.extend([rid] * count)
         depths.extend([depth] * count)
@@ -255,21 +255,23 @@ def make_prefill(dtype):
                                  dtype=np.int32),
     }
     for layer in range(2):
-        k = values(rng, (len(ids), 2, 64), dtype)
-        v = values(rng, (len(ids), 2, 64), dtype)
-        q = values(rng, (len(ids), 4, 64), dtype)
+        k = values(rng, (len(ids), 2, d), dtype)
+        v = values(rng, (len(ids), 2, d), dtype)
+        q = values(rng, (len(ids), 4, d), dtype)
         cache._write_prepared(layer, batch, k, v)
         expected = torch_paged_attention(q, cache.key_cache[:, layer], cache.value_cache[:, layer],
                                          flat.block_tables, flat.context_lengths)
-        out[f"k{layer}"] = storage(k)
-        out[f"v{layer}"] = storage(v)
-        out[f"q{layer}"] = storage(q)
+        if store_inputs:  # otherwise re-drawn from the seeded generator by the test
+            out[f"k{layer}"] = storage(k)
+            out[f"v{layer}"] = storage(v)
+            out[f"q{layer}"] = storage(q)
         out[f"out{layer}"] = storage(expected)
     out["key_digest"] = np.array(digest(cache.key_cache))
     out["value_digest"] = np.array(digest(cache.value_cache))
     out["prefix_seed"] = np.array([712, 2])
-    np.savez_compressed(HERE / f"prefill_{dtype}.npz", **out)
-    print(f"prefill_{dtype}: {len(ids)} tokens")
+    out["geometry"] = np.array([d, blocks, max_tokens])
+    np.savez_compressed(HERE / f"prefill{tag}_{dtype}.npz", **out)
+    print(f"prefill{tag}_{dtype}: {len(ids)} tokens")
 
 
 def make_routing():
@@ -381,6 +383,10 @@ def main():
         make_long(dtype)
         make_shared(dtype)
         make_prefill(dtype)
+    for dtype in ("f16", "bf16"):
+        # head_dim 128, chunks crossing 128-query tiles, prefixes crossing pages
+        make_prefill(dtype, d=128, spec=[("a", 0, 0, 150), ("b", 2, 17, 7), ("c", 3, 131, 260)],
+                     max_tokens=400, blocks=400, tag="128", store_inputs=False)
     make_routing()
 
 

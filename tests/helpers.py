@@ -136,3 +136,40 @@ def assert_close(actual, expected, dtype: str, **override):
             f"max abs err {err.max():.3e}; first at {tuple(idx)}: {a[tuple(idx)]} vs {b[tuple(idx)]}"
         )
     return float(err.max()) if err.size else 0.0
+
+
+def prefill_names() -> list[str]:
+    return sorted(p.stem for p in GOLDEN.glob("prefill*.npz"))
+
+
+def prefill_case(name: str, writer_factory):
+    """Rebuild a packed-prefill scenario: prefix writes (drawn from the
+    recorded seed), then per layer the chunk's k, v, q (stored in the fixture
+    or re-drawn in the order make_golden.py drew them). Returns the fixture,
+    the writer holding the prefix pool and the per-layer inputs."""
+    fx = load(name)
+    dtype = str(fx["dtype"])
+    d, blocks, _ = (int(x) for x in fx["geometry"]) if "geometry" in fx else (64, 80, 65)
+    writer = writer_factory((blocks, 2, 16, 2, d), dtype)
+    rng = np.random.default_rng(fx["prefix_seed"].tolist())
+
+    def draw(shape):
+        return oracle.from_f32(rng.standard_normal(shape, dtype=np.float32), dtype)
+
+    for rid, depth, prefix, count in fx["spec"].tolist():
+        for layer in range(2):
+            if prefix:
+                kv = draw((prefix, 2, d))
+                neg = oracle.from_f32(-oracle.to_f32(kv, dtype), dtype)
+                for p in range(prefix):
+                    writer.write(layer, int(fx["alloc_tables"][rid, depth, p // 16]), p % 16,
+                                 kv[p], neg[p])
+    n = int(fx["cu_seqlens_q"][-1])
+    inputs = []
+    for layer in range(2):
+        if f"k{layer}" in fx:
+            inputs.append((fx[f"k{layer}"], fx[f"v{layer}"], fx[f"q{layer}"]))
+        else:
+            k, v, q = draw((n, 2, d)), draw((n, 2, d)), draw((n, 4, d))
+            inputs.append((k, v, q))
+    return fx, writer, inputs

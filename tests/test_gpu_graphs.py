@@ -89,9 +89,10 @@ def test_decode_and_kv_write_capture_replay_matches_eager():
     assert backend.check_errors() == []
 
 
-def test_prefill_and_routing_capture():
+@pytest.mark.parametrize("d", [64, 128])  # CUDA-core path, tensor-core path
+def test_prefill_capture(d):
     torch.manual_seed(1)
-    page, hkv, d = 16, 4, 64
+    page, hkv = 16, 4
     key = torch.randn(64, 1, page, hkv, d, device="cuda").to(torch.float16)
     value = torch.randn_like(key)
     tables = torch.arange(64, dtype=torch.int32, device="cuda").view(4, 16)

@@ -11,46 +11,43 @@ import torch
 import oracle
 import vllm_rlt_b200 as rb
 from gpu_helpers import TORCH, CudaWriter, to_numpy, to_torch
-from helpers import assert_close, digest, load
+from helpers import assert_close, digest, prefill_case, prefill_names
+from vllm_rlt_b200 import _lib
 
 pytestmark = pytest.mark.gpu
 
 
-def rebuild(dtype):
-    fx = load(f"prefill_{dtype}")
-    writer = CudaWriter((80, 2, 16, 2, 64), dtype)
-    rng = np.random.default_rng(fx["prefix_seed"].tolist())
-    for rid, depth, prefix, count in fx["spec"].tolist():
-        for layer in range(2):
-            if prefix:
-                kv = oracle.from_f32(rng.standard_normal((prefix, 2, 64), dtype=np.float32), dtype)
-                neg = oracle.from_f32(-oracle.to_f32(kv, dtype), dtype)
-                for p in range(prefix):
-                    writer.write(layer, int(fx["alloc_tables"][rid, depth, p // 16]), p % 16,
-                                 kv[p], neg[p])
+@pytest.mark.parametrize("name", prefill_names())
+def test_packed_prefill_matches_reference(name):
+    fx, writer, inputs = prefill_case(name, CudaWriter)
     writer.flush()
-    return fx, writer
-
-
-@pytest.mark.parametrize("dtype", ["f32", "f16", "bf16"])
-def test_packed_prefill_matches_reference(dtype):
-    fx, writer = rebuild(dtype)
+    dtype = str(fx["dtype"])
+    d = inputs[0][2].shape[-1]
     blocks = torch.from_numpy(fx["write_blocks"]).cuda()
     offsets = torch.from_numpy(fx["write_offsets"]).cuda()
-    backend = rb.B200PagedAttention("cuda", TORCH[dtype], 64, 16)
-    for layer in range(2):
-        rb.write_kv(writer.key, writer.value, layer, blocks, offsets,
-                    to_torch(fx[f"k{layer}"], dtype), to_torch(fx[f"v{layer}"], dtype))
-        out = backend.prefill(to_torch(fx[f"q{layer}"], dtype), writer.key[:, layer],
-                              writer.value[:, layer], torch.from_numpy(fx["block_tables"]).cuda(),
+    backend = rb.B200PagedAttention("cuda", TORCH[dtype], d, 16)
+    for layer, (k, v, q) in enumerate(inputs):
+        rb.write_kv(writer.key, writer.value, layer, blocks, offsets, to_torch(k, dtype),
+                    to_torch(v, dtype))
+        out = backend.prefill(to_torch(q, dtype), writer.key[:, layer], writer.value[:, layer],
+                              torch.from_numpy(fx["block_tables"]).cuda(),
                               torch.from_numpy(fx["context_lengths"]).cuda(),
                               torch.from_numpy(fx["cu_seqlens_q"]).cuda(), int(fx["max_seqlen_q"]))
         torch.cuda.synchronize()
+        assert backend.check_errors() == []
         assert_close(to_numpy(out), fx[f"out{layer}"], dtype)
     key, value = writer.numpy()
     assert digest(key) == str(fx["key_digest"])
     assert digest(value) == str(fx["value_digest"])
-    assert backend.check_errors() == []
+
+
+def test_tensor_core_path_selection():
+    lib = _lib.load()
+    assert lib.rlt_paged_prefill_uses_tensor_cores(_lib.BF16, 128, 16) == 1
+    assert lib.rlt_paged_prefill_uses_tensor_cores(_lib.F16, 128, 32) == 1
+    assert lib.rlt_paged_prefill_uses_tensor_cores(_lib.F32, 128, 16) == 0
+    assert lib.rlt_paged_prefill_uses_tensor_cores(_lib.BF16, 64, 16) == 0
+    assert lib.rlt_paged_prefill_uses_tensor_cores(_lib.BF16, 128, 5) == 0
 
 
 @pytest.mark.parametrize("dtype", ["bf16", "f16"])

@@ -13,8 +13,8 @@ import numpy as np
 import pytest
 
 import oracle
-from helpers import (NumpyWriter, assert_close, digest, load, query_inputs, replay_pool,
-                     scenario_names)
+from helpers import (NumpyWriter, assert_close, digest, load, prefill_case, prefill_names,
+                     query_inputs, replay_pool, scenario_names)
 from vllm_rlt_b200 import workloads
 
 SCENARIOS = scenario_names()
@@ -88,25 +88,10 @@ def test_config1_plan_matches_reference_allocator(dtype):
     np.testing.assert_array_equal(plan.context_lengths, fx["q0_context_lengths"])
 
 
-def rebuild_prefill(dtype):
-    fx = load(f"prefill_{dtype}")
-    writer = NumpyWriter((80, 2, 16, 2, 64), dtype)
-    rng = np.random.default_rng(fx["prefix_seed"].tolist())
-    for rid, depth, prefix, count in fx["spec"].tolist():
-        for layer in range(2):
-            if prefix:
-                kv = rng.standard_normal((prefix, 2, 64), dtype=np.float32)
-                kv = oracle.from_f32(kv, dtype)
-                neg = oracle.from_f32(-oracle.to_f32(kv, dtype), dtype)
-                blocks = [fx["alloc_tables"][rid, depth, p // 16] for p in range(prefix)]
-                offsets = [p % 16 for p in range(prefix)]
-                oracle.kv_write(writer.key, writer.value, layer, blocks, offsets, kv, neg)
-    return fx, writer
-
-
-@pytest.mark.parametrize("dtype", ["f32", "f16", "bf16"])
-def test_oracle_packed_prefill_matches_reference(dtype):
-    fx, writer = rebuild_prefill(dtype)
+@pytest.mark.parametrize("name", prefill_names())
+def test_oracle_packed_prefill_matches_reference(name):
+    fx, writer, inputs = prefill_case(name, NumpyWriter)
+    dtype = str(fx["dtype"])
     spec = fx["spec"].tolist()
     tables = {rid: [list(fx["alloc_tables"][rid, p]) for p in range(4)] for rid, _, _, _ in spec}
     ids, depths, positions = [], [], []
@@ -121,10 +106,10 @@ def test_oracle_packed_prefill_matches_reference(dtype):
     np.testing.assert_array_equal(packed["cu_seqlens_q"], fx["cu_seqlens_q"])
     np.testing.assert_array_equal(packed["write_blocks"], fx["write_blocks"])
     np.testing.assert_array_equal(packed["write_offsets"], fx["write_offsets"])
-    for layer in range(2):
+    for layer, (k, v, q) in enumerate(inputs):
         oracle.kv_write(writer.key, writer.value, layer, fx["write_blocks"], fx["write_offsets"],
-                        fx[f"k{layer}"], fx[f"v{layer}"])
-        out = oracle.paged_prefill(fx[f"q{layer}"], writer.key[:, layer], writer.value[:, layer],
+                        k, v)
+        out = oracle.paged_prefill(q, writer.key[:, layer], writer.value[:, layer],
                                    fx["block_tables"], fx["context_lengths"], fx["cu_seqlens_q"],
                                    dtype)
         tight = dict(atol=1e-6, rtol=1e-6, ulps=0) if dtype == "f32" else {}

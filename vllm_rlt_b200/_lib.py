@@ -37,6 +37,7 @@ STATUS_BITS = {
     4: "in-page offset outside [0, page)",
     8: "descriptor slot/depth/position outside the resident tables",
     16: "packed-prefill metadata inconsistent",
+    32: "a bounded wait in a tensor-core kernel timed out",
 }
 
 _i32, _i64, _f32, _sz, _p = (
@@ -64,6 +65,7 @@ SIGNATURES = {
         _i32,
         [_p] * 8 + [_sz, _p, _i32] + [_i32] * 8 + [_i64] * 12 + [_f32, _p],
     ),
+    "rlt_paged_prefill_uses_tensor_cores": (_i32, [_i32, _i32, _i32]),
     "rlt_kv_write": (_i32, [_p] * 7 + [_i32] * 6 + [_i64] * 9 + [_p]),
     "rlt_finalize": (_i32, [_p] * 5 + [_i32] * 8 + [_i64] * 4 + [_p]),
     "rlt_metadata": (_i32, [_p] * 9 + [_i32] * 7 + [_p]),

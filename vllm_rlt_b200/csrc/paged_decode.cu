@@ -55,12 +55,16 @@ struct SplitPlan {
   int per;    // tokens per split (multiple of kSplitAlign)
 };
 
-// A function of the row's own length only (never of the batch or the launch
-// shape), which keeps every row's reduction order batch-invariant.
-__host__ __device__ __forceinline__ SplitPlan split_plan(int ctx) {
+// For decode, a function of the row's own length only: the cap `max_splits`
+// is the launch's split count, derived from the table width so that it is at
+// least min(ceil(len / chunk), kMaxSplits) for every row the table can hold.
+// Every row's reduction order is therefore batch-invariant. The packed-prefill
+// path launches a single split (max_splits = 1).
+__host__ __device__ __forceinline__ SplitPlan split_plan(int ctx, int max_splits) {
   if (ctx <= 0) return {0, 0};
   int n = (ctx + kSplitChunk - 1) / kSplitChunk;
   if (n > kMaxSplits) n = kMaxSplits;
+  if (n > max_splits) n = max_splits;
   int per = (ctx + n - 1) / n;
   per = (per + kSplitAlign - 1) / kSplitAlign * kSplitAlign;
   return {(ctx + per - 1) / per, per};
@@ -139,7 +143,7 @@ __global__ void __launch_bounds__(kDecodeWarps * 32, 4)
     }
     return;
   }
-  const SplitPlan plan = split_plan(ctx);
+  const SplitPlan plan = split_plan(ctx, p.launch_splits);
   if (split >= plan.count) return;
   const int start = split * plan.per;
   const int end = min(ctx, start + plan.per);
@@ -364,7 +368,7 @@ __global__ void __launch_bounds__(256) decode_combine_kernel(const __grid_consta
   const int row = blockIdx.x;
   const int qh = blockIdx.y;
   const int ctx = checked_length(p, row, false);
-  const SplitPlan plan = split_plan(ctx);
+  const SplitPlan plan = split_plan(ctx, p.launch_splits);
   if (plan.count <= 1) return;
   const int64_t base = static_cast<int64_t>(row) * p.launch_splits * p.hq + qh;
   float mx = -INFINITY;
@@ -631,6 +635,17 @@ int run(DecodeParams p, int32_t dtype, bool fast, void* split_ws, cudaStream_t s
 namespace rlt {
 namespace detail {
 
+constexpr int kNotEligible = 1;
+
+// Tensor-core packed prefill (paged_prefill_tc.cu); kNotEligible when the
+// shape is outside what it covers.
+int paged_prefill_tc(const void* q, const void* key_cache, const void* value_cache,
+                     const int32_t* block_tables, const int32_t* context_lengths,
+                     const int32_t* cu_seqlens_q, void* out, int32_t* status, int32_t dtype,
+                     int32_t num_tokens, int32_t num_seqs, int32_t hq, int32_t hkv,
+                     int32_t head_dim, int32_t page, int32_t width, int64_t num_blocks,
+                     const int64_t* st, float scale, cudaStream_t stream);
+
 // Decode with caller-provided split scratch of `capacity` bytes (the static
 // scratch of the no-allocation entry point). Same kernels, same split plan
 // and therefore the same results as rlt_paged_decode.
@@ -702,9 +717,15 @@ extern "C" int rlt_paged_decode(const void* q, const void* key_cache, const void
 extern "C" size_t rlt_paged_prefill_workspace_bytes(int32_t num_tokens, int32_t num_q_heads,
                                                     int32_t head_dim, int32_t page_size,
                                                     int32_t table_width) {
+  (void)num_q_heads;
+  (void)head_dim;
+  (void)page_size;
+  (void)table_width;
   if (num_tokens <= 0) return 0;
-  return align16(static_cast<size_t>(num_tokens) * 2 * sizeof(int32_t)) +
-         split_bytes(num_tokens, num_q_heads, head_dim, page_size, table_width);
+  // Per-token (table row, causal length) pairs. The CUDA-core path runs one
+  // split per token row (thousands of rows already fill the GPU), so it
+  // needs no split partials; the tensor-core path needs no scratch at all.
+  return align16(static_cast<size_t>(num_tokens) * 2 * sizeof(int32_t));
 }
 
 extern "C" int rlt_paged_prefill(const void* q, const void* key_cache, const void* value_cache,
@@ -721,6 +742,9 @@ extern "C" int rlt_paged_prefill(const void* q, const void* key_cache, const voi
                                  int64_t table_row_stride, int64_t out_row_stride,
                                  int64_t out_head_stride, float scale, void* stream) {
   (void)max_seqlen_q;  // the launch shape never depends on host-known lengths
+  const int64_t strides[11] = {q_row_stride,     q_head_stride,  k_block_stride, k_token_stride,
+                               k_head_stride,    v_block_stride, v_token_stride, v_head_stride,
+                               table_row_stride, out_row_stride, out_head_stride};
   const DecodeArgs a{q, key_cache, value_cache, block_tables, status, dtype, num_tokens,
                      num_q_heads, num_kv_heads, head_dim, page_size, table_width, num_blocks,
                      q_row_stride, q_head_stride, k_block_stride, k_token_stride, k_head_stride,
@@ -735,11 +759,14 @@ extern "C" int rlt_paged_prefill(const void* q, const void* key_cache, const voi
                                                         page_size, table_width);
   if (workspace == nullptr || workspace_bytes < need || !aligned16(workspace))
     return RLT_E_WORKSPACE;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const int tc = detail::paged_prefill_tc(q, key_cache, value_cache, block_tables, context_lengths,
+                                          cu_seqlens_q, out, status, dtype, num_tokens, num_seqs,
+                                          num_q_heads, num_kv_heads, head_dim, page_size,
+                                          table_width, num_blocks, strides, scale, s);
+  if (tc != detail::kNotEligible) return tc;
   int32_t* row_seq = static_cast<int32_t*>(workspace);
   int32_t* row_len = row_seq + num_tokens;
-  void* split_ws =
-      static_cast<char*>(workspace) + align16(static_cast<size_t>(num_tokens) * 2 * sizeof(int32_t));
-  cudaStream_t s = static_cast<cudaStream_t>(stream);
   prefill_rows_kernel<<<ceil_div(num_tokens, 256), 256, 0, s>>>(
       cu_seqlens_q, context_lengths, row_seq, row_len, status, num_tokens, num_seqs);
   cudaError_t err = cudaGetLastError();
@@ -748,5 +775,6 @@ extern "C" int rlt_paged_prefill(const void* q, const void* key_cache, const voi
   DecodeParams p = make_params(a, &fast);
   p.lengths = row_len;
   p.table_index = row_seq;
-  return run(p, dtype, fast, split_ws, s);
+  p.launch_splits = 1;
+  return run(p, dtype, fast, nullptr, s);
 }

@@ -1,0 +1,508 @@
+// Packed chunked-prefill paged causal attention on the sm_100a tensor cores.
+//
+// Semantics (vllm_rlt/kernels/flash_attention.py:66-96, FA4 varlen with a
+// page table, causal, bottom-right aligned): sequence s owns query tokens
+// cu[s] .. cu[s+1]-1 and keys 0 .. len_s-1 through its block table; query i
+// of the chunk (0-based) sees keys 0 .. len_s - qlen_s + i.
+//
+// One CTA = (128-query tile of one sequence, one query head), 4 warps:
+//  * TMA (tiled, never multicast) brings the Q tile and, per 128-key tile,
+//    each K/V page of the head (a 4-D tensor map over the strided layer view
+//    [blocks, page, Hkv, D]) into 128-byte-swizzled shared memory; pages past
+//    the context or with a bad id are fetched at an out-of-range coordinate,
+//    which the TMA unit fills with zeros;
+//  * thread 0 issues tcgen05.mma: S = Q K^T (M=128, N=128, K=128) into TMEM
+//    columns [0,128), then O += P V into TMEM columns [128,256);
+//  * each thread owns one query row: it reads its S row with tcgen05.ld,
+//    applies the causal mask and the scale, keeps a base-2 running max that
+//    is only moved (and O rescaled in TMEM) when it grows by more than 2^8,
+//    and writes P (input dtype) into swizzled shared memory for the PV MMA;
+//  * K/V are double-buffered; every mbarrier wait is bounded and reports
+//    RLT_STATUS_TIMEOUT instead of hanging.
+#include <cudaTypedefs.h>
+
+#include <mutex>
+
+#include "common.cuh"
+#include "tc_ptx.cuh"
+
+namespace rlt {
+namespace {
+
+constexpr int kTileM = 128;
+constexpr int kTileN = 128;
+constexpr int kHeadDim = 128;
+constexpr int kThreads = 128;
+constexpr uint32_t kTmemCols = 256;       // S: [0, 128), O: [128, 256)
+constexpr int kHalfBytes = 128 * 128;     // 128 rows x 64 columns x 2 B
+constexpr int kTileBytes = 2 * kHalfBytes;
+constexpr int kSmemBytes = 6 * kTileBytes + 1024;  // Q, K x2, V x2, P + alignment slack
+constexpr long long kWaitLimit = 100000000LL;      // cycles (~50 ms at 1.9 GHz)
+constexpr int32_t kStatusTimeout = 32;
+
+struct PrefillTcParams {
+  CUtensorMap qmap;  // {D, Hq, tokens}, box {64, 1, 128}
+  CUtensorMap kmap;  // {D, Hkv, page, blocks}, box {64, 1, page, 1}
+  CUtensorMap vmap;
+  const int32_t* tables;
+  const int32_t* lengths;
+  const int32_t* cu;
+  void* out;
+  int32_t* status;
+  int num_seqs, num_tokens, hq, group, page, width;
+  int64_t num_blocks, t_rs, o_rs, o_hs;
+  float scale_log2;
+};
+
+// Byte offset of 16-byte chunk c of row r inside one [128 rows x 128 B]
+// half-tile stored with the 128-byte swizzle (chunk index XOR row % 8).
+__device__ __forceinline__ uint32_t sw128(int r, int c) {
+  return static_cast<uint32_t>((r >> 3) * 1024 + (r & 7) * 128 + ((c ^ (r & 7)) << 4));
+}
+
+template <typename T>
+__device__ __forceinline__ uint32_t pack2(float lo, float hi);
+template <>
+__device__ __forceinline__ uint32_t pack2<__nv_bfloat16>(float lo, float hi) {
+  __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
+  return *reinterpret_cast<uint32_t*>(&v);
+}
+template <>
+__device__ __forceinline__ uint32_t pack2<__half>(float lo, float hi) {
+  __half2 v = __floats2half2_rn(lo, hi);
+  return *reinterpret_cast<uint32_t*>(&v);
+}
+
+template <typename T>
+struct Fmt;
+template <>
+struct Fmt<__half> {
+  static constexpr uint32_t value = 0;
+};
+template <>
+struct Fmt<__nv_bfloat16> {
+  static constexpr uint32_t value = 1;
+};
+
+// Warp 0: map blockIdx.x to (sequence, first query of the tile) by a running
+// prefix over ceil(qlen_s / 128). Returns seq = -1 past the last tile.
+__device__ void find_tile(const int32_t* cu, int num_seqs, int target, int lane, int* seq_out,
+                          int* m0_out) {
+  int running = 0;
+  for (int base = 0; base < num_seqs; base += 32) {
+    const int s = base + lane;
+    int tiles = 0;
+    if (s < num_seqs) {
+      const int qlen = cu[s + 1] - cu[s];
+      tiles = qlen > 0 ? (qlen + kTileM - 1) / kTileM : 0;
+    }
+    int incl = tiles;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int y = __shfl_up_sync(kFullMask, incl, o);
+      if (lane >= o) incl += y;
+    }
+    const int excl = running + incl - tiles;
+    const bool mine = s < num_seqs && target >= excl && target < excl + tiles;
+    const unsigned hit = __ballot_sync(kFullMask, mine);
+    if (mine) {
+      *seq_out = s;
+      *m0_out = (target - excl) * kTileM;
+    }
+    if (hit) return;
+    running += __shfl_sync(kFullMask, incl, 31);
+  }
+  if (lane == 0) {
+    *seq_out = -1;
+    *m0_out = 0;
+  }
+}
+
+template <typename T>
+__global__ void __launch_bounds__(kThreads, 1)
+    paged_prefill_tc_kernel(const __grid_constant__ PrefillTcParams p) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~static_cast<uintptr_t>(1023));
+  uint8_t* sQ = smem;
+  uint8_t* sK[2] = {smem + kTileBytes, smem + 2 * kTileBytes};
+  uint8_t* sV[2] = {smem + 3 * kTileBytes, smem + 4 * kTileBytes};
+  uint8_t* sP = smem + 5 * kTileBytes;
+
+  __shared__ __align__(8) uint64_t bar_q, bar_kv[2], bar_s, bar_pv;
+  __shared__ uint32_t tmem_base_sh;
+  __shared__ int tile_seq, tile_m0, abort_flag;
+
+  const int tid = threadIdx.x;
+  const int warp = tid >> 5;
+  const int lane = tid & 31;
+  const int head = blockIdx.y;
+  const int kvh = head / p.group;
+
+  if (warp == 0) find_tile(p.cu, p.num_seqs, blockIdx.x, lane, &tile_seq, &tile_m0);
+  if (tid == 0) {
+    tc::mbar_init(&bar_q, 1);
+    tc::mbar_init(&bar_kv[0], 1);
+    tc::mbar_init(&bar_kv[1], 1);
+    tc::mbar_init(&bar_s, 1);
+    tc::mbar_init(&bar_pv, 1);
+    tc::fence_mbar_init();
+    abort_flag = 0;
+  }
+  __syncwarp();
+  if (warp == 0) tc::tmem_alloc(&tmem_base_sh, kTmemCols);  // warp-collective
+  tc::tc_fence_before();
+  __syncthreads();
+  tc::tc_fence_after();
+  const uint32_t tmem = tmem_base_sh;
+  const uint32_t s_tmem = tmem;
+  const uint32_t o_tmem = tmem + kTileN;
+  const uint32_t lane_base = static_cast<uint32_t>(warp * 32) << 16;
+
+  int seq = tile_seq;
+  const int m0 = tile_m0;
+  int qbegin = 0, qlen = 0, ctx = 0, n_tiles = 0;
+  if (seq >= 0) {
+    qbegin = p.cu[seq];
+    qlen = p.cu[seq + 1] - qbegin;
+    ctx = p.lengths[seq];
+    if (qbegin < 0 || qlen <= 0 || qbegin + qlen > p.num_tokens || ctx < 0 ||
+        static_cast<int64_t>(ctx) > static_cast<int64_t>(p.width) * p.page) {
+      if (tid == 0) raise_status(p.status, kStatusBadSequence);
+      seq = -1;
+    } else {
+      const int kmax = ctx - qlen + min(qlen - 1, m0 + kTileM - 1);
+      n_tiles = kmax >= 0 ? kmax / kTileN + 1 : 0;
+    }
+  }
+
+  const int pages_per_tile = kTileN / p.page;
+  int issued = -1;  // last K/V tile whose loads thread 0 issued
+  auto load_kv = [&](int t) {
+    const int st = t & 1;
+    tc::mbar_expect_tx(&bar_kv[st], 2 * kTileBytes);
+    for (int pg = 0; pg < pages_per_tile; ++pg) {
+      const int logical = t * pages_per_tile + pg;
+      int blk = static_cast<int>(p.num_blocks);  // out of range: zero fill
+      if (logical * p.page < ctx) {
+        const int b = p.tables[seq * p.t_rs + logical];
+        if (b >= 0 && b < p.num_blocks)
+          blk = b;
+        else
+          raise_status(p.status, kStatusBadBlock);
+      }
+      const int row_off = pg * p.page * 128;
+#pragma unroll
+      for (int dh = 0; dh < 2; ++dh) {
+        tc::tma_load_4d(sK[st] + dh * kHalfBytes + row_off, &p.kmap, &bar_kv[st], dh * 64, kvh,
+                        0, blk);
+        tc::tma_load_4d(sV[st] + dh * kHalfBytes + row_off, &p.vmap, &bar_kv[st], dh * 64, kvh,
+                        0, blk);
+      }
+    }
+    issued = t;
+  };
+
+  const int qi = m0 + tid;  // this thread's query row within the sequence chunk
+  const int row_limit = min(ctx - qlen + qi, ctx - 1);
+  float m_used = -INFINITY;
+  float l_sum = 0.f;
+  const uint32_t idesc_qk = tc::idesc_f16(Fmt<T>::value, kTileM, kTileN, 0);
+  const uint32_t idesc_pv = tc::idesc_f16(Fmt<T>::value, kTileM, kHeadDim, 1);
+  int done_tiles = 0;
+  int s_commits = 0, pv_commits = 0;  // thread 0: commits issued on bar_s / bar_pv
+
+  if (seq >= 0 && n_tiles > 0) {
+    if (tid == 0) {
+      tc::mbar_expect_tx(&bar_q, kTileBytes);
+      tc::tma_load_3d(sQ, &p.qmap, &bar_q, 0, head, qbegin + m0);
+      tc::tma_load_3d(sQ + kHalfBytes, &p.qmap, &bar_q, 64, head, qbegin + m0);
+      load_kv(0);
+      if (n_tiles > 1) load_kv(1);
+      if (!tc::mbar_wait(&bar_q, 0, kWaitLimit)) abort_flag = 1;
+    }
+    for (int t = 0; t < n_tiles; ++t) {
+      const int st = t & 1;
+      if (tid == 0 && !abort_flag) {
+        if (tc::mbar_wait(&bar_kv[st], (t >> 1) & 1, kWaitLimit)) {
+          tc::tc_fence_after();
+#pragma unroll
+          for (int ks = 0; ks < kHeadDim / 16; ++ks) {
+            const uint32_t off = (ks >> 2) * kHalfBytes + (ks & 3) * 32;
+            tc::mma_f16_ss(s_tmem, tc::smem_desc_sw128(tc::smem_u32(sQ) + off, 16, 1024),
+                           tc::smem_desc_sw128(tc::smem_u32(sK[st]) + off, 16, 1024), idesc_qk,
+                           ks > 0);
+          }
+          tc::mma_commit(&bar_s);
+          ++s_commits;
+        } else {
+          abort_flag = 1;
+        }
+      }
+      __syncthreads();
+      if (abort_flag) break;
+      if (!tc::mbar_wait(&bar_s, t & 1, kWaitLimit)) abort_flag = 1;
+      tc::tc_fence_after();
+
+      // ---- softmax on this thread's S row (128 keys)
+      uint32_t sr[4][32];
+#pragma unroll
+      for (int c = 0; c < 4; ++c) tc::tmem_ld32(s_tmem + lane_base + c * 32, sr[c]);
+#pragma unroll
+      for (int c = 0; c < 4; ++c) tc::tmem_ld_wait(sr[c]);
+      const int n0 = t * kTileN;
+      float mx = -INFINITY;
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+#pragma unroll
+        for (int j = 0; j < 32; ++j) {
+          const int key = n0 + c * 32 + j;
+          const float s = key <= row_limit ? __uint_as_float(sr[c][j]) * p.scale_log2 : -INFINITY;
+          sr[c][j] = __float_as_uint(s);
+          mx = fmaxf(mx, s);
+        }
+      }
+      const float m_new = fmaxf(m_used, mx);
+      float factor = 1.f;
+      if (m_new > m_used + 8.f) {  // includes the first finite max (m_used = -inf)
+        factor = ex2(m_used - m_new);
+        m_used = m_new;
+      }
+      const float mref = m_used == -INFINITY ? 0.f : m_used;
+      uint32_t packed[64];
+      float psum = 0.f;
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+#pragma unroll
+        for (int j = 0; j < 32; j += 2) {
+          const float p0 = ex2(__uint_as_float(sr[c][j]) - mref);
+          const float p1 = ex2(__uint_as_float(sr[c][j + 1]) - mref);
+          psum += p0 + p1;
+          packed[c * 16 + j / 2] = pack2<T>(p0, p1);
+        }
+      }
+      l_sum = l_sum * factor + psum;
+
+      // PV of the previous tile must be done before P is overwritten and O
+      // is rescaled; it also frees the K/V stage for tile t + 1.
+      if (t > 0) {
+        if (!tc::mbar_wait(&bar_pv, (t - 1) & 1, kWaitLimit)) abort_flag = 1;
+        tc::tc_fence_after();
+        if (tid == 0 && t + 1 < n_tiles && !abort_flag) load_kv(t + 1);
+        // tcgen05.ld/st are warp-collective (.sync.aligned): the whole warp
+        // rescales when any of its rows moved its max (factor is 1 elsewhere).
+        if (__any_sync(kFullMask, factor != 1.f)) {
+#pragma unroll
+          for (int c = 0; c < 4; ++c) {
+            uint32_t o[32];
+            tc::tmem_ld32(o_tmem + lane_base + c * 32, o);
+            tc::tmem_ld_wait(o);
+#pragma unroll
+            for (int j = 0; j < 32; ++j) o[j] = __float_as_uint(__uint_as_float(o[j]) * factor);
+            tc::tmem_st32(o_tmem + lane_base + c * 32, o);
+          }
+          tc::tmem_st_wait();
+        }
+      }
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+#pragma unroll
+        for (int c = 0; c < 8; ++c) {
+          const int base = h * 32 + c * 4;
+          *reinterpret_cast<uint4*>(sP + h * kHalfBytes + sw128(tid, c)) =
+              make_uint4(packed[base], packed[base + 1], packed[base + 2], packed[base + 3]);
+        }
+      }
+      tc::fence_proxy_async_smem();
+      tc::tc_fence_before();
+      __syncthreads();
+      if (abort_flag) break;
+      if (tid == 0) {
+        tc::tc_fence_after();
+#pragma unroll
+        for (int ks = 0; ks < kTileN / 16; ++ks) {
+          const uint32_t aoff = (ks >> 2) * kHalfBytes + (ks & 3) * 32;
+          tc::mma_f16_ss(o_tmem, tc::smem_desc_sw128(tc::smem_u32(sP) + aoff, 16, 1024),
+                         tc::smem_desc_sw128(tc::smem_u32(sV[st]) + ks * 2048, kHalfBytes, 1024),
+                         idesc_pv, (t > 0 || ks > 0) ? 1u : 0u);
+        }
+        tc::mma_commit(&bar_pv);
+        ++pv_commits;
+      }
+      done_tiles = t + 1;
+    }
+    if (done_tiles == n_tiles && !abort_flag) {
+      if (!tc::mbar_wait(&bar_pv, (n_tiles - 1) & 1, kWaitLimit)) abort_flag = 1;
+      tc::tc_fence_after();
+    }
+  }
+  __syncthreads();
+  if (abort_flag) {
+    // Give in-flight copies and MMAs a bounded chance to land before the
+    // shared memory and TMEM are released.
+    if (tid == 0) {
+      raise_status(p.status, kStatusTimeout);
+      for (int t = done_tiles; t <= issued; ++t)
+        tc::mbar_wait(&bar_kv[t & 1], (t >> 1) & 1, kWaitLimit);
+      if (s_commits > 0) tc::mbar_wait(&bar_s, (s_commits - 1) & 1, kWaitLimit);
+      if (pv_commits > 0) tc::mbar_wait(&bar_pv, (pv_commits - 1) & 1, kWaitLimit);
+    }
+  } else if (seq >= 0) {
+    // seq and n_tiles are uniform over the CTA, so every warp reads its TMEM
+    // lanes with all 32 threads; only rows inside the chunk are stored.
+    const bool store = qi < qlen;
+    T* dst = static_cast<T*>(p.out) + (qbegin + (store ? qi : 0)) * p.o_rs + head * p.o_hs;
+    const float inv = l_sum > 0.f ? 1.f / l_sum : 0.f;
+#pragma unroll
+    for (int c = 0; c < 4; ++c) {
+      uint32_t o[32];
+      if (n_tiles > 0) {
+        tc::tmem_ld32(o_tmem + lane_base + c * 32, o);
+        tc::tmem_ld_wait(o);
+      } else {
+#pragma unroll
+        for (int j = 0; j < 32; ++j) o[j] = 0u;
+      }
+      if (!store) continue;
+#pragma unroll
+      for (int v = 0; v < 4; ++v) {
+        uint4 w;
+        w.x = pack2<T>(__uint_as_float(o[v * 8 + 0]) * inv, __uint_as_float(o[v * 8 + 1]) * inv);
+        w.y = pack2<T>(__uint_as_float(o[v * 8 + 2]) * inv, __uint_as_float(o[v * 8 + 3]) * inv);
+        w.z = pack2<T>(__uint_as_float(o[v * 8 + 4]) * inv, __uint_as_float(o[v * 8 + 5]) * inv);
+        w.w = pack2<T>(__uint_as_float(o[v * 8 + 6]) * inv, __uint_as_float(o[v * 8 + 7]) * inv);
+        *reinterpret_cast<uint4*>(dst + c * 32 + v * 8) = w;
+      }
+    }
+  }
+  tc::tc_fence_before();
+  __syncthreads();
+  if (warp == 0) {
+    tc::tc_fence_after();
+    tc::tmem_dealloc(tmem, kTmemCols);
+  }
+}
+
+// ---- host side --------------------------------------------------------------
+
+PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* ptr = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(ptr);
+  });
+  return fn;
+}
+
+bool encode(CUtensorMap* map, CUtensorMapDataType type, uint32_t rank, const void* base,
+            const uint64_t* dims, const uint64_t* strides_bytes, const uint32_t* box) {
+  auto fn = encode_fn();
+  if (fn == nullptr) return false;
+  const uint32_t elem[4] = {1, 1, 1, 1};
+  return fn(map, type, rank, const_cast<void*>(base), dims, strides_bytes, box, elem,
+            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+            CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) ==
+         CUDA_SUCCESS;
+}
+
+bool aligned16(const void* ptr) { return (reinterpret_cast<uintptr_t>(ptr) & 15u) == 0; }
+
+}  // namespace
+
+namespace detail {
+
+constexpr int kNotEligible = 1;
+
+bool prefill_tc_shape(int32_t dtype, int32_t head_dim, int32_t page) {
+  return (dtype == RLT_BF16 || dtype == RLT_F16) && head_dim == kHeadDim &&
+         (page == 8 || page == 16 || page == 32 || page == 64 || page == 128);
+}
+
+// Launch the tensor-core prefill when the shape fits it; kNotEligible leaves
+// the call to the CUDA-core path.
+int paged_prefill_tc(const void* q, const void* key_cache, const void* value_cache,
+                     const int32_t* block_tables, const int32_t* context_lengths,
+                     const int32_t* cu_seqlens_q, void* out, int32_t* status, int32_t dtype,
+                     int32_t num_tokens, int32_t num_seqs, int32_t hq, int32_t hkv,
+                     int32_t head_dim, int32_t page, int32_t width, int64_t num_blocks,
+                     const int64_t* st, float scale, cudaStream_t stream) {
+  // st: q_rs, q_hs, k_bs, k_ts, k_hs, v_bs, v_ts, v_hs, t_rs, o_rs, o_hs (elements)
+  if (!prefill_tc_shape(dtype, head_dim, page)) return kNotEligible;
+  if (num_blocks <= 0 || num_blocks >= INT32_MAX || num_seqs <= 0) return kNotEligible;
+  if (!aligned16(q) || !aligned16(key_cache) || !aligned16(value_cache) || !aligned16(out))
+    return kNotEligible;
+  for (int i = 0; i < 11; ++i)
+    if (i != 8 && (st[i] * 2) % 16) return kNotEligible;
+  if (st[0] <= 0 || st[1] <= 0 || st[2] <= 0 || st[3] <= 0 || st[4] <= 0 || st[5] <= 0 ||
+      st[6] <= 0 || st[7] <= 0)
+    return kNotEligible;
+
+  PrefillTcParams p{};
+  const CUtensorMapDataType type =
+      dtype == RLT_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+  {
+    const uint64_t dims[3] = {static_cast<uint64_t>(head_dim), static_cast<uint64_t>(hq),
+                              static_cast<uint64_t>(num_tokens)};
+    const uint64_t strides[2] = {static_cast<uint64_t>(st[1]) * 2, static_cast<uint64_t>(st[0]) * 2};
+    const uint32_t box[3] = {64, 1, kTileM};
+    if (!encode(&p.qmap, type, 3, q, dims, strides, box)) return kNotEligible;
+  }
+  {
+    const uint64_t dims[4] = {static_cast<uint64_t>(head_dim), static_cast<uint64_t>(hkv),
+                              static_cast<uint64_t>(page), static_cast<uint64_t>(num_blocks)};
+    const uint32_t box[4] = {64, 1, static_cast<uint32_t>(page), 1};
+    const uint64_t ks[3] = {static_cast<uint64_t>(st[4]) * 2, static_cast<uint64_t>(st[3]) * 2,
+                            static_cast<uint64_t>(st[2]) * 2};
+    const uint64_t vs[3] = {static_cast<uint64_t>(st[7]) * 2, static_cast<uint64_t>(st[6]) * 2,
+                            static_cast<uint64_t>(st[5]) * 2};
+    if (!encode(&p.kmap, type, 4, key_cache, dims, ks, box)) return kNotEligible;
+    if (!encode(&p.vmap, type, 4, value_cache, dims, vs, box)) return kNotEligible;
+  }
+  p.tables = block_tables;
+  p.lengths = context_lengths;
+  p.cu = cu_seqlens_q;
+  p.out = out;
+  p.status = status;
+  p.num_seqs = num_seqs;
+  p.num_tokens = num_tokens;
+  p.hq = hq;
+  p.group = hq / hkv;
+  p.page = page;
+  p.width = width;
+  p.num_blocks = num_blocks;
+  p.t_rs = st[8];
+  p.o_rs = st[9];
+  p.o_hs = st[10];
+  p.scale_log2 = scale * 1.4426950408889634f;
+
+  static std::once_flag attr_once[2];
+  const int which = dtype == RLT_BF16 ? 1 : 0;
+  cudaError_t attr_err = cudaSuccess;
+  std::call_once(attr_once[which], [&] {
+    attr_err = dtype == RLT_BF16
+                   ? cudaFuncSetAttribute(paged_prefill_tc_kernel<__nv_bfloat16>,
+                                          cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes)
+                   : cudaFuncSetAttribute(paged_prefill_tc_kernel<__half>,
+                                          cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
+  });
+  if (attr_err != cudaSuccess) return static_cast<int>(attr_err);
+  const dim3 grid(static_cast<unsigned>((num_tokens + kTileM - 1) / kTileM + num_seqs), hq);
+  if (dtype == RLT_BF16)
+    paged_prefill_tc_kernel<__nv_bfloat16><<<grid, kThreads, kSmemBytes, stream>>>(p);
+  else
+    paged_prefill_tc_kernel<__half><<<grid, kThreads, kSmemBytes, stream>>>(p);
+  return launch_status(cudaGetLastError());
+}
+
+}  // namespace detail
+}  // namespace rlt
+
+extern "C" int rlt_paged_prefill_uses_tensor_cores(int32_t dtype, int32_t head_dim,
+                                                   int32_t page_size) {
+  return rlt::detail::prefill_tc_shape(dtype, head_dim, page_size) ? 1 : 0;
+}
