@@ -52,6 +52,10 @@ def parse():
     p.add_argument("--impl", choices=["ours", "reference"], default="ours")
     p.add_argument("--rows", type=int, default=256)
     p.add_argument("--no-cpu-baseline", action="store_true")
+    p.add_argument("--no-extras", action="store_true",
+                   help="skip the prefill and long-context sub-measurements")
+    p.add_argument("--workload", choices=["decode", "prefill", "longctx"], default="decode",
+                   help="decode: the headline line; prefill/longctx: that workload alone")
     return p.parse_args()
 
 
@@ -61,6 +65,13 @@ def measured_peak():
         data = json.loads(path.read_text())
         return float(data["hbm_gbs"]), "measured"
     return FALLBACK_HBM_GBS, "fallback"
+
+
+def measured_tensor_peak():
+    path = ROOT / "MEASURED_PEAKS.json"
+    if path.exists():
+        return float(json.loads(path.read_text())["bf16_tflops"]), "measured (burst)"
+    return 1590.0, "fallback (burst)"
 
 
 def committed_traffic():
@@ -217,6 +228,137 @@ def run_reference(args):
     print(json.dumps(line), flush=True)
 
 
+# ------------------------------------------------------------------ extras
+
+
+def fill_random(t, g):
+    """Fill a (large) tensor with N(0,1) in chunks, bounding the fp32 temporary."""
+    import torch
+
+    flat = t.view(-1)
+    step = 1 << 28
+    for s in range(0, flat.numel(), step):
+        n = min(step, flat.numel() - s)
+        flat[s : s + n].copy_(torch.randn(n, generator=g, device=t.device))
+
+
+def time_region(fn, steps, warmup, device):
+    """Device time of `steps` calls of fn() after `warmup` calls (CUDA events)."""
+    import torch
+
+    for _ in range(warmup):
+        fn()
+    torch.cuda.synchronize(device)
+    a = torch.cuda.Event(enable_timing=True)
+    b = torch.cuda.Event(enable_timing=True)
+    a.record()
+    for _ in range(steps):
+        fn()
+    b.record()
+    torch.cuda.synchronize(device)
+    return a.elapsed_time(b) / steps
+
+
+def prefill_extra(device, steps, warmup, rank):
+    """chunked prefill of 64 prompts (uniform 512..8192, chunk
+    2048, shared leading pages up to 50%) on the tensor-core kernel."""
+    import torch
+
+    import vllm_rlt_b200 as rb
+    from vllm_rlt_b200 import workloads
+
+    plan = workloads.config4_plan(seed=100 + rank)
+    g = torch.Generator(device=device).manual_seed(7 + rank)
+    key = torch.empty((plan.num_blocks, 1, 16, 16, 128), device=device, dtype=torch.bfloat16)
+    value = torch.empty_like(key)
+    fill_random(key, g)
+    fill_random(value, g)
+    tables_all = torch.from_numpy(plan.tables).to(device)
+    rounds = []
+    for active, starts, lengths in plan.rounds():
+        cu = np.concatenate([[0], np.cumsum(lengths)]).astype(np.int32)
+        q = torch.empty((int(cu[-1]), 16, 128), device=device, dtype=torch.bfloat16)
+        fill_random(q, g)
+        rounds.append(dict(
+            q=q, tables=tables_all[torch.from_numpy(active).to(device)].contiguous(),
+            lengths=torch.from_numpy((starts + lengths).astype(np.int32)).to(device),
+            cu=torch.from_numpy(cu).to(device), max_q=int(lengths.max())))
+    backend = rb.B200PagedAttention(device, torch.bfloat16, 128, 16)
+
+    def step():
+        for r in rounds:
+            backend.prefill(r["q"], key[:, 0], value[:, 0], r["tables"], r["lengths"], r["cu"],
+                            r["max_q"])
+
+    ms = time_region(step, steps, warmup, device)
+    errors = backend.check_errors()
+    peak, kind = measured_tensor_peak()
+    tflops = plan.flops() / (ms / 1e3) / 1e12
+    tc = rb._lib.load().rlt_paged_prefill_uses_tensor_cores(rb._lib.BF16, 128, 16)
+    return {
+        "workload": "configs[3]: 64 prompts U[512,8192], chunk 2048, prefix pages U[0,50%], "
+                    "bf16 16x128, page 16",
+        "ms_per_step": round(ms, 3), "chunk_rounds": len(rounds),
+        "tokens_per_step": int((plan.prompt_lengths - plan.reused).sum()),
+        "value": round(tflops, 1), "unit": "TFLOP/s (causal pairs x 4 x D x Hq)",
+        "roofline": {"bound": "tensor", "achieved": round(tflops, 1), "peak": peak,
+                     "unit": "TFLOP/s", "frac": round(tflops / peak, 4), "peak_kind": kind},
+        "path": "tcgen05" if tc else "cuda-core", "errors": errors,
+    }
+
+
+def longctx_extra(device, steps, warmup, rank, world):
+    """long-context skewed decode, SHARED layout, 64 rows per GPU,
+    Pareto(1.5) contexts in [1024, 32768], split-KV; the 64 x world requests
+    are assigned to ranks by greedy LPT on KV bytes."""
+    import torch
+
+    import vllm_rlt_b200 as rb
+    from vllm_rlt_b200 import workloads
+    from vllm_rlt_b200.kernels.paged_attention import decode_bytes
+
+    full = workloads.config5_plan(seed=0, rows=64 * world)
+    kv = full.context_lengths.astype(np.int64) * 16 * 128 * 2 * 2
+    parts = workloads.lpt_assign(kv, world)
+    mine = np.array(sorted(parts[rank]), dtype=np.int64)
+    loads = [int(kv[p].sum()) for p in parts]
+    lengths = full.context_lengths[mine]
+    pages = [int(math.ceil(int(n) / 16)) for n in lengths]
+    num_blocks = sum(pages)
+    width = max(pages)
+    tables = np.full((len(mine), width), -1, dtype=np.int32)
+    perm = np.random.default_rng(1 + rank).permutation(num_blocks)
+    c = 0
+    for i, n in enumerate(pages):
+        tables[i, :n] = perm[c : c + n]
+        c += n
+    g = torch.Generator(device=device).manual_seed(11 + rank)
+    key = torch.empty((num_blocks, 1, 16, 16, 128), device=device, dtype=torch.bfloat16)
+    value = torch.empty_like(key)
+    fill_random(key, g)
+    fill_random(value, g)
+    q = torch.empty((len(mine), 16, 128), device=device, dtype=torch.bfloat16)
+    fill_random(q, g)
+    t_tables = torch.from_numpy(tables).to(device)
+    t_lengths = torch.from_numpy(lengths.astype(np.int32)).to(device)
+    backend = rb.B200PagedAttention(device, torch.bfloat16, 128, 16)
+    ms = time_region(lambda: backend(q, key[:, 0], value[:, 0], t_tables, t_lengths), steps,
+                     warmup, device)
+    step_bytes = decode_bytes(lengths, 16, 16, 128, 2)
+    peak, kind = measured_peak()
+    gbs = step_bytes / (ms / 1e3) / 1e9
+    return {
+        "workload": "configs[4]: SHARED layout, Pareto(1.5) ctx in [1024, 32768], 64 rows/GPU, "
+                    "split-KV, LPT by KV bytes across ranks",
+        "rows": int(len(mine)), "sum_ctx": int(lengths.sum()), "max_ctx": int(lengths.max()),
+        "ms_per_step": round(ms, 4), "value": round(gbs, 1), "unit": "GB/s",
+        "roofline": {"bound": "hbm", "achieved": round(gbs, 1), "peak": peak, "unit": "GB/s",
+                     "frac": round(gbs / peak, 4), "peak_kind": kind},
+        "rank_kv_bytes_max_over_mean": round(max(loads) / (sum(loads) / len(loads)), 4),
+        "errors": backend.check_errors(),
+    }
+
+
 # ------------------------------------------------------------------ ours
 
 
@@ -239,19 +381,27 @@ def run_ours(args):
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
                                 device_id=device)
 
+    if args.workload != "decode":
+        if args.workload == "prefill":
+            res = prefill_extra(device, args.steps, args.warmup, rank)
+        else:
+            res = longctx_extra(device, args.steps, args.warmup, rank, world)
+        if world > 1:
+            dist.barrier(device_ids=[local])
+            dist.destroy_process_group()
+        if rank == 0:
+            print(json.dumps({"workload_line": args.workload, "n_gpus": world, **res}), flush=True)
+        return
+
     # Each rank serves its own request shard (seed = rank): weak scaling.
     plan = workloads.config2_plan(seed=rank, rows=args.rows)
     g = torch.Generator(device=device).manual_seed(1000 + rank)
     shape = (plan.num_blocks, 1, plan.page, plan.num_kv_heads, plan.head_dim)
-    key = torch.empty(shape, device=device, dtype=torch.bfloat16)
-    value = torch.empty_like(key)
-    for t in (key, value):  # fill in chunks to bound the fp32 temporary
-        flat = t.view(-1)
-        step = 1 << 28
-        for s in range(0, flat.numel(), step):
-            n = min(step, flat.numel() - s)
-            flat[s : s + n].copy_(torch.randn(n, generator=g, device=device))
-    k_layer, v_layer = key[:, 0], value[:, 0]
+    kpool = torch.empty(shape, device=device, dtype=torch.bfloat16)
+    vpool = torch.empty_like(kpool)
+    fill_random(kpool, g)
+    fill_random(vpool, g)
+    k_layer, v_layer = kpool[:, 0], vpool[:, 0]
     tables_np = plan.block_tables()
     tables = torch.from_numpy(tables_np).to(device)
     lengths = torch.from_numpy(plan.context_lengths).to(device)
@@ -360,6 +510,18 @@ def run_ours(args):
                        "numpy restatement of the reference's torch path, fp32 math"),
         }
 
+    extras = {}
+    if not args.no_extras:
+        # free the decode pool first: the extras allocate their own pools
+        del kpool, vpool, k_layer, v_layer
+        torch.cuda.empty_cache()
+        for name, fn in (("prefill", lambda: prefill_extra(device, 10, 3, rank)),
+                         ("longctx", lambda: longctx_extra(device, 20, 5, rank, world))):
+            try:
+                extras[name] = fn()
+            except Exception as error:  # reported, never silently dropped
+                extras[name] = {"error": f"{type(error).__name__}: {error}"}
+
     if world > 1:
         dist.barrier(device_ids=[local])
         dist.destroy_process_group()
@@ -408,6 +570,8 @@ def run_ours(args):
     }
     if cpu is not None:
         line["cpu_baseline"] = cpu
+    if extras:
+        line["extras"] = extras
     print(json.dumps(line), flush=True)
 
 

@@ -28,10 +28,23 @@
 namespace rlt {
 namespace {
 
-constexpr int kDecodeWarps = 4;     // warps (= warp tasks) per CTA
-constexpr int kSplitAlign = 32;     // every split starts at a multiple of this
-constexpr int kSplitChunk = 256;    // target tokens per split
-constexpr int kMaxSplits = 32;      // cap; longer rows get longer splits
+// Tunables (compile-time; the defaults are the measured best on B200).
+#ifndef RLT_DECODE_WARPS
+#define RLT_DECODE_WARPS 4
+#endif
+#ifndef RLT_DECODE_MIN_BLOCKS
+#define RLT_DECODE_MIN_BLOCKS 5
+#endif
+#ifndef RLT_DECODE_V_EARLY
+#define RLT_DECODE_V_EARLY 1
+#endif
+#ifndef RLT_DECODE_SPLIT_CHUNK
+#define RLT_DECODE_SPLIT_CHUNK 256
+#endif
+constexpr int kDecodeWarps = RLT_DECODE_WARPS;       // warps (= warp tasks) per CTA
+constexpr int kSplitAlign = 32;                      // every split starts at a multiple of this
+constexpr int kSplitChunk = RLT_DECODE_SPLIT_CHUNK;  // target tokens per split
+constexpr int kMaxSplits = 32;                       // cap; longer rows get longer splits
 
 struct DecodeParams {
   const void* q;
@@ -103,7 +116,7 @@ __device__ __forceinline__ int checked_length(const DecodeParams& p, int row, bo
 }
 
 template <typename T, int D, int GC, bool ALIGNED>
-__global__ void __launch_bounds__(kDecodeWarps * 32, 4)
+__global__ void __launch_bounds__(kDecodeWarps * 32, RLT_DECODE_MIN_BLOCKS)
     paged_decode_kernel(const __grid_constant__ DecodeParams p) {
   constexpr int VEC = Vec16<T>::kElems;
   constexpr int LPT = D / VEC;  // lanes per token row
@@ -232,6 +245,7 @@ __global__ void __launch_bounds__(kDecodeWarps * 32, 4)
       }
     }
 
+#if RLT_DECODE_V_EARLY
     // Issue the V loads now so they overlap the reductions below.
     uint4 vr[TOK];
     if constexpr (ALIGNED) {
@@ -247,6 +261,7 @@ __global__ void __launch_bounds__(kDecodeWarps * 32, 4)
       }
     }
 
+#endif
     // Butterfly reduce-scatter across the LPT lanes of the group: after step
     // k each lane keeps half of its partials, so lane s ends with token s>>PLAIN.
 #pragma unroll
@@ -277,6 +292,23 @@ __global__ void __launch_bounds__(kDecodeWarps * 32, 4)
       valid = __shfl_sync(kFullMask, my_k, g * LPT + tl) >= 0;
     }
 
+#if !RLT_DECODE_V_EARLY
+    // Issue the V loads after the reductions (lower register pressure).
+    uint4 vr[TOK];
+    if constexpr (ALIGNED) {
+#pragma unroll
+      for (int j = 0; j < TOK; ++j)
+        vr[j] = (page_ok && t0 + j < end) ? ld_stream(vbase + vp + j * p.v_ts) : zero4;
+    } else {
+#pragma unroll
+      for (int j = 0; j < TOK; ++j) {
+        const int64_t kj = __shfl_sync(kFullMask, my_k, g * LPT + j);
+        const int64_t vj = __shfl_sync(kFullMask, my_v, g * LPT + j);
+        vr[j] = kj >= 0 ? ld_stream(vbase + vj) : zero4;
+      }
+    }
+
+#endif
     // Online softmax (base 2) over the warp's ITOK tokens.
 #pragma unroll
     for (int c = 0; c < GC; ++c) {

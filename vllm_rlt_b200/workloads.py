@@ -141,3 +141,77 @@ def write_schedule(plan: DecodePlan):
                 yield ("write", r, depth, p)
             yield ("finalize", r, p, e)
         yield ("write", r, int(plan.query_depths[r]), pos)
+
+
+@dataclass
+class PrefillPlan:
+    """Chunked prefill of many prompts over one paged pool."""
+
+    prompt_lengths: np.ndarray  # int64 [requests]
+    reused: np.ndarray  # int64 [requests], reused prefix tokens (whole pages)
+    tables: np.ndarray  # int32 [requests, width]; leading pages shared with a donor
+    num_blocks: int
+    chunk: int
+    page: int = 16
+    num_q_heads: int = 16
+    num_kv_heads: int = 16
+    head_dim: int = 128
+
+    def rounds(self):
+        """Per chunk round: (request ids, chunk starts, chunk lengths)."""
+        starts = self.reused.copy()
+        while True:
+            active = np.nonzero(starts < self.prompt_lengths)[0]
+            if len(active) == 0:
+                return
+            lengths = np.minimum(self.chunk, self.prompt_lengths[active] - starts[active])
+            yield active, starts[active].copy(), lengths
+            starts[active] += lengths
+
+    def causal_pairs(self) -> int:
+        """Query-key pairs attended: sum over computed positions i of (i + 1)."""
+        length = self.prompt_lengths.astype(np.int64)
+        s = self.reused.astype(np.int64)
+        return int(((length * (length + 1) - s * (s + 1)) // 2).sum())
+
+    def flops(self) -> int:
+        return 4 * self.head_dim * self.num_q_heads * self.causal_pairs()
+
+
+def config4_plan(seed: int = 0, requests: int = 64, chunk: int = 2048) -> PrefillPlan:
+    """64 prompts with lengths uniform in [512, 8192], chunk 2048,
+    bf16 16x128 heads, page 16; each request's number of shared leading pages
+    is uniform in [0, 50%] of its pages and those pages point at one donor's
+    pages (prefix reuse: they are attended, not recomputed)."""
+    rng = np.random.default_rng(seed)
+    page = 16
+    lengths = rng.integers(512, 8193, size=requests).astype(np.int64)
+    pages = (lengths + page - 1) // page
+    shared = np.array([rng.integers(0, p // 2 + 1) for p in pages], dtype=np.int64)
+    shared = np.minimum(shared, (lengths - 1) // page)  # at least one token to compute
+    donor = int(shared.max())
+    num_blocks = donor + int((pages - shared).sum())
+    order = rng.permutation(num_blocks)
+    donor_pages, fresh = order[:donor], order[donor:]
+    width = int(pages.max())
+    tables = np.full((requests, width), -1, dtype=np.int32)
+    cursor = 0
+    for r in range(requests):
+        tables[r, : shared[r]] = donor_pages[: shared[r]]
+        own = int(pages[r] - shared[r])
+        tables[r, shared[r] : pages[r]] = fresh[cursor : cursor + own]
+        cursor += own
+    return PrefillPlan(lengths, shared * page, tables, num_blocks, chunk)
+
+
+def lpt_assign(kv_bytes, ranks: int):
+    """Greedy longest-processing-time assignment of requests to ranks by KV
+    bytes: returns a list of request-index lists, one per rank."""
+    order = np.argsort(-np.asarray(kv_bytes), kind="stable")
+    loads = [0] * ranks
+    parts = [[] for _ in range(ranks)]
+    for i in order:
+        r = min(range(ranks), key=lambda k: (loads[k], k))
+        parts[r].append(int(i))
+        loads[r] += int(kv_bytes[i])
+    return parts
