@@ -54,7 +54,8 @@ def parse():
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--no-extras", action="store_true",
                    help="skip the prefill and long-context sub-measurements")
-    p.add_argument("--workload", choices=["decode", "prefill", "longctx"], default="decode",
+    p.add_argument("--workload", choices=["decode", "prefill", "longctx", "ouro"],
+                   default="decode",
                    help="decode: the headline line; prefill/longctx: that workload alone")
     return p.parse_args()
 
@@ -359,6 +360,73 @@ def longctx_extra(device, steps, warmup, rank, world):
     }
 
 
+def ouro_extra(device, steps, warmup, rank, requests=64):
+    """random-init Ouro-1.4B-shaped mixed-depth decode. 64 resident
+    requests per GPU (LAST-EXITED needs ~1.6 GB of KV per request at 4 planes
+    x 24 layers, so 512 requests are reached at 8 GPUs), contexts uniform in
+    [256, 4096], per-token exit depth uniform in {1..4}; one step = one
+    CUDA-graph replay of the recurrent core at every request's own depth."""
+    import torch
+
+    from vllm_rlt_b200.ouro import (DecodeScheduler, OuroDecoder, OuroShape, OuroWeights,
+                                    decode_bytes_per_pass)
+
+    rng = np.random.default_rng(50 + rank)
+    shape = OuroShape()
+    ctx = rng.integers(256, 4097, size=requests).astype(np.int64)
+    exits = rng.integers(0, 4, size=(requests, 4 * (steps + warmup) + 8))
+    weights = OuroWeights(shape, device, torch.bfloat16, seed=rank)
+    dec = OuroDecoder(shape, weights, ctx + steps + warmup + 8, device, torch.bfloat16,
+                      seed=rank)
+    g = torch.Generator(device=device).manual_seed(60 + rank)
+    for pool in (dec.key_cache, dec.value_cache):  # synthetic history for every plane
+        flat = pool.view(-1)
+        for s0 in range(0, flat.numel(), 1 << 30):
+            flat[s0 : s0 + (1 << 30)].normal_(generator=g)
+    sched = DecodeScheduler(dec, ctx, lambda slot, i: int(exits[slot, i]))
+    exiting = sched.prepare()
+    dec.capture()
+    dec.run()
+    sched.advance(exiting)
+    for _ in range(warmup):
+        exiting = sched.prepare()
+        dec.run()
+        sched.advance(exiting)
+    torch.cuda.synchronize(device)
+    a = torch.cuda.Event(enable_timing=True)
+    b = torch.cuda.Event(enable_timing=True)
+    generated0 = sched.generated
+    step_bytes = 0
+    a.record()
+    for _ in range(steps):
+        step_bytes += decode_bytes_per_pass(shape, sched.pos + 1)
+        exiting = sched.prepare()
+        dec.run()
+        sched.advance(exiting)
+    b.record()
+    torch.cuda.synchronize(device)
+    ms = a.elapsed_time(b)
+    tokens = sched.generated - generated0
+    errors = dec.attention.check_errors()
+    peak, kind = measured_peak()
+    gbs = step_bytes / (ms / 1e3) / 1e9
+    kv_gb = (dec.key_cache.numel() + dec.value_cache.numel()) * 2 / 1e9
+    del dec, weights
+    torch.cuda.empty_cache()
+    return {
+        "workload": "configs[2]: Ouro-1.4B-shaped (24 layers x 4 loops, 2048 hidden, 16x128 "
+                    "heads, SwiGLU 5632, vocab 49152, RoPE 1e4, bf16, random init), 64 requests "
+                    "per GPU, ctx U[256,4096], exit depth U{1..4}, LAST-EXITED, graph-captured step",
+        "tok_s_per_gpu": round(tokens / (ms / 1e3), 1), "tokens": int(tokens),
+        "steps": steps, "ms_per_step": round(ms / steps, 3),
+        "kv_pool_gb": round(kv_gb, 1),
+        "hbm": {"achieved": round(gbs, 1), "peak": peak, "unit": "GB/s",
+                "frac": round(gbs / peak, 4), "peak_kind": kind,
+                "bytes": "per pass: every layer's K/V of every row's context + core weights"},
+        "errors": errors,
+    }
+
+
 # ------------------------------------------------------------------ ours
 
 
@@ -384,6 +452,8 @@ def run_ours(args):
     if args.workload != "decode":
         if args.workload == "prefill":
             res = prefill_extra(device, args.steps, args.warmup, rank)
+        elif args.workload == "ouro":
+            res = ouro_extra(device, args.steps, args.warmup, rank)
         else:
             res = longctx_extra(device, args.steps, args.warmup, rank, world)
         if world > 1:
@@ -515,12 +585,14 @@ def run_ours(args):
         # free the decode pool first: the extras allocate their own pools
         del kpool, vpool, k_layer, v_layer
         torch.cuda.empty_cache()
-        for name, fn in (("prefill", lambda: prefill_extra(device, 10, 3, rank)),
+        for name, fn in (("ouro", lambda: ouro_extra(device, 30, 3, rank)),
+                         ("prefill", lambda: prefill_extra(device, 10, 3, rank)),
                          ("longctx", lambda: longctx_extra(device, 20, 5, rank, world))):
             try:
                 extras[name] = fn()
             except Exception as error:  # reported, never silently dropped
                 extras[name] = {"error": f"{type(error).__name__}: {error}"}
+            torch.cuda.empty_cache()
 
     if world > 1:
         dist.barrier(device_ids=[local])
