@@ -222,6 +222,40 @@ int rlt_gather(const void* pool, const int64_t* slots, void* out, int32_t n, int
 int rlt_scatter(const void* values, const int64_t* slots, void* pool, int32_t n, int32_t width,
                 int32_t elem_bytes, int64_t in_stride, int64_t out_stride, void* stream);
 
+/* ---- fused per-layer glue of the recurrent core (calling context) ---- */
+
+/* RMSNorm over rows of `hidden` elements with the reference's rounding:
+ * y = weight * to_dtype(x * rsqrt(mean(x^2) + eps)) in fp32; if residual is
+ * not NULL, out = residual + y (rounded to the dtype). hidden <= 4096.
+ * Replaces: vllm_rlt/models/ouro.py:33-36 (OuroRMSNorm.forward) and the
+ * residual adds of the decoder layer at :143-147. */
+int rlt_rms_norm(const void* x, const void* weight, const void* residual, void* out,
+                 int32_t dtype, int32_t rows, int32_t hidden, float eps, int64_t x_stride,
+                 int64_t residual_stride, int64_t out_stride, void* stream);
+
+/* RoPE on q and k straight out of the fused qkv projection, k written (with
+ * v) into the KV page of its depth plane:
+ *   angles = pos * inv_freq (fp32); cos/sin rounded to the dtype;
+ *   x' = x * cos + rotate_half(x) * sin (each op rounded to the dtype);
+ *   q_out[r] = q'; key_cache[blocks[r], layer, offsets[r]] = k'; value_cache[..] = v.
+ * qkv rows hold [heads*D | kv_heads*D | kv_heads*D]. Bit-identical to the
+ * unfused torch expression followed by rlt_kv_write.
+ * Replaces: vllm_rlt/models/ouro.py:61-75 and :104-110 plus the page write of
+ * vllm_rlt/core/kv_cache_manager.py:531-532. */
+int rlt_rope_write_kv(const void* qkv, const int64_t* positions, const float* inv_freq,
+                      void* q_out, void* key_cache, void* value_cache,
+                      const int64_t* write_blocks, const int64_t* write_offsets, int32_t* status,
+                      int32_t dtype, int32_t rows, int32_t heads, int32_t kv_heads,
+                      int32_t head_dim, int32_t layer, int32_t page_size, int64_t num_blocks,
+                      int64_t qkv_stride, int64_t q_row_stride, int64_t q_head_stride,
+                      int64_t cache_block_stride, int64_t cache_layer_stride,
+                      int64_t cache_token_stride, int64_t cache_head_stride, void* stream);
+
+/* SwiGLU: out = silu(gate) * up with gate_up rows [gate | up] (each op rounded
+ * to the dtype). Replaces: vllm_rlt/models/ouro.py:122-123. */
+int rlt_silu_mul(const void* gate_up, void* out, int32_t dtype, int32_t rows,
+                 int32_t intermediate, int64_t in_stride, int64_t out_stride, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -144,3 +144,68 @@ def test_graph_replay_matches_eager_steps():
         s2.advance(exiting)
     assert torch.equal(eager.key_cache, graphed.key_cache)
     assert torch.equal(eager.value_cache, graphed.value_cache)
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16, torch.float32])
+def test_fused_rope_kv_write_is_bit_identical_to_torch(dtype):
+    from vllm_rlt_b200 import write_kv
+    from vllm_rlt_b200.kernels import ouro_ops
+
+    torch.manual_seed(0)
+    heads, kv_heads, d, n = 16, 4, 128, 37
+    qkv = torch.randn(n, (heads + 2 * kv_heads) * d, device="cuda").to(dtype) * 3
+    positions = torch.randint(0, 70000, (n,), device="cuda")
+    inv_freq = 1.0 / (10000.0 ** (torch.arange(0, d, 2, device="cuda", dtype=torch.float32) / d))
+    pool = torch.zeros(40, 3, 16, kv_heads, d, device="cuda", dtype=dtype)
+    vpool = torch.zeros_like(pool)
+    blocks = torch.randperm(40, device="cuda")[:n].sort().values
+    offsets = torch.randint(0, 16, (n,), device="cuda")
+    q = ouro_ops.rope_write_kv(qkv, positions, inv_freq, pool, vpool, 1, blocks, offsets, heads,
+                               kv_heads, d)
+    # the unfused expression of vllm_rlt/models/ouro.py:61-75, :104-110
+    angles = positions.float().unsqueeze(-1) * inv_freq
+    angles = torch.cat((angles, angles), dim=-1)
+    cos, sin = angles.cos().to(dtype).unsqueeze(1), angles.sin().to(dtype).unsqueeze(1)
+    q_ref = qkv[:, : heads * d].view(n, heads, d)
+    k_ref = qkv[:, heads * d : (heads + kv_heads) * d].view(n, kv_heads, d)
+    v_ref = qkv[:, (heads + kv_heads) * d :].view(n, kv_heads, d)
+    q_ref = q_ref * cos + rotate_half(q_ref) * sin
+    k_ref = k_ref * cos + rotate_half(k_ref) * sin
+    pool_ref, vpool_ref = torch.zeros_like(pool), torch.zeros_like(vpool)
+    write_kv(pool_ref, vpool_ref, 1, blocks, offsets, k_ref, v_ref)
+    torch.cuda.synchronize()
+    assert torch.equal(q, q_ref)
+    assert torch.equal(pool, pool_ref) and torch.equal(vpool, vpool_ref)
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float32])
+def test_fused_norm_and_swiglu_match_torch(dtype):
+    from vllm_rlt_b200.kernels import ouro_ops
+
+    torch.manual_seed(1)
+    x = torch.randn(19, 2048, device="cuda").to(dtype)
+    res = torch.randn(19, 2048, device="cuda").to(dtype)
+    w = (1 + 0.1 * torch.randn(2048, device="cuda")).to(dtype)
+    got = ouro_ops.rms_norm(x, w, 1e-6, residual=res)
+    want = res + rms_norm(x, w, 1e-6)
+    tol = dict(atol=0, rtol=2**-7) if dtype == torch.bfloat16 else dict(atol=1e-5, rtol=1e-5)
+    torch.testing.assert_close(got, want, **tol)
+    gu = torch.randn(19, 2 * 5632, device="cuda").to(dtype) * 4
+    got = ouro_ops.silu_mul(gu, 5632)
+    want = torch.nn.functional.silu(gu[:, :5632]) * gu[:, 5632:]
+    torch.testing.assert_close(got, want, **tol)
+
+
+def test_fused_decoder_matches_unfused_decoder():
+    fused, s1 = make_decoder(torch.float32, seed=5)
+    plain, s2 = make_decoder(torch.float32, seed=5)
+    plain.fused = False
+    for _ in range(8):
+        e1, e2 = s1.prepare(), s2.prepare()
+        fused.run(graphed=False)
+        plain.run(graphed=False)
+        torch.cuda.synchronize()
+        torch.testing.assert_close(fused.hidden_state, plain.hidden_state, atol=1e-5, rtol=1e-5)
+        assert torch.equal(fused.tokens, plain.tokens)
+        s1.advance(e1)
+        s2.advance(e2)

@@ -1,0 +1,213 @@
+// Fused per-layer glue of the Ouro recurrent core (sm_100a):
+//  * RMSNorm (optionally with the residual add that follows it),
+//  * RoPE on q and k fused with the KV page write into the depth plane,
+//  * SwiGLU activation.
+// Each reproduces the rounding steps of the reference's torch expressions
+// (vllm_rlt/models/ouro.py): every torch op on a 16-bit tensor computes in
+// fp32 and rounds its result to the tensor dtype, so the fused kernels round
+// at the same points.
+#include "common.cuh"
+
+namespace rlt {
+namespace {
+
+template <typename T>
+__device__ __forceinline__ float rnd(float x) {  // round to T and back (one torch op's output)
+  return to_f32<T>(from_f32<T>(x));
+}
+
+// One torch elementwise op = one IEEE-rounded fp32 operation (then rounded to
+// T): the explicit _rn intrinsics keep the compiler from contracting a
+// multiply and an add into one fused multiply-add, which rounds once.
+__device__ __forceinline__ float mul(float a, float b) { return __fmul_rn(a, b); }
+__device__ __forceinline__ float add(float a, float b) { return __fadd_rn(a, b); }
+
+// vllm_rlt/models/ouro.py:33-36:
+//   value = x.float(); value = value * rsqrt(mean(value^2) + eps)
+//   y = weight * value.to(dtype)            (then, fused: residual + y)
+// One CTA per row; the row is cached in registers (hidden <= 32 * 8 * 16).
+template <typename T>
+__global__ void __launch_bounds__(256) rms_norm_kernel(const T* __restrict__ x, const T* __restrict__ w,
+                                                       const T* __restrict__ residual, T* __restrict__ out,
+                                                       int hidden, float eps, int64_t x_stride,
+                                                       int64_t r_stride, int64_t o_stride) {
+  const int row = blockIdx.x;
+  const T* xr = x + row * x_stride;
+  float vals[16];
+  float ss = 0.f;
+#pragma unroll
+  for (int i = 0; i < 16; ++i) {
+    const int c = threadIdx.x + i * blockDim.x;
+    vals[i] = c < hidden ? to_f32<T>(xr[c]) : 0.f;
+    ss = fmaf(vals[i], vals[i], ss);
+  }
+  __shared__ float partial[32];
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(kFullMask, ss, o);
+  if ((threadIdx.x & 31) == 0) partial[threadIdx.x >> 5] = ss;
+  __syncthreads();
+  if (threadIdx.x < 32) {
+    float t = threadIdx.x < (blockDim.x >> 5) ? partial[threadIdx.x] : 0.f;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) t += __shfl_xor_sync(kFullMask, t, o);
+    if (threadIdx.x == 0) partial[0] = t;
+  }
+  __syncthreads();
+  const float inv = rsqrtf(partial[0] / static_cast<float>(hidden) + eps);
+  T* orow = out + row * o_stride;
+  const T* rrow = residual ? residual + row * r_stride : nullptr;
+#pragma unroll
+  for (int i = 0; i < 16; ++i) {
+    const int c = threadIdx.x + i * blockDim.x;
+    if (c >= hidden) continue;
+    float y = rnd<T>(mul(to_f32<T>(w[c]), rnd<T>(mul(vals[i], inv))));
+    if (rrow) y = add(to_f32<T>(rrow[c]), y);
+    orow[c] = from_f32<T>(y);
+  }
+}
+
+// vllm_rlt/models/ouro.py:61-75 and :104-110, fused with the page write of
+// vllm_rlt/core/kv_cache_manager.py:531-532:
+//   angles = pos.float() * inv_freq  (fp32), cat(angles, angles)
+//   cos, sin = angles.cos().to(dtype), angles.sin().to(dtype)
+//   q' = q * cos + rotate_half(q) * sin  (each op rounded to dtype), same for k
+//   key_cache[block, layer, offset] = k'; value_cache[...] = v
+// grid = rows, block = (heads + kv_heads) * head_dim / 2 pairs, capped.
+template <typename T>
+__global__ void __launch_bounds__(256) rope_write_kernel(
+    const T* __restrict__ qkv, const int64_t* __restrict__ positions,
+    const float* __restrict__ inv_freq, T* __restrict__ q_out, T* __restrict__ kc,
+    T* __restrict__ vc, const int64_t* __restrict__ blocks, const int64_t* __restrict__ offsets,
+    int32_t* status, int heads, int kv_heads, int head_dim, int layer, int page,
+    int64_t num_blocks, int64_t qkv_stride, int64_t q_rs, int64_t q_hs, int64_t c_bs,
+    int64_t c_ls, int64_t c_ts, int64_t c_hs) {
+  const int row = blockIdx.x;
+  const int half = head_dim / 2;
+  const float pos = static_cast<float>(positions[row]);
+  const T* src = qkv + row * qkv_stride;
+  const int64_t blk = blocks[row];
+  const int64_t off = offsets[row];
+  const bool ok = blk >= 0 && blk < num_blocks && off >= 0 && off < page;
+  if (!ok && threadIdx.x == 0)
+    raise_status(status, (blk < 0 || blk >= num_blocks) ? kStatusBadBlock : kStatusBadOffset);
+  const int64_t cache_row = blk * c_bs + layer * c_ls + off * c_ts;
+  const int rotated = (heads + kv_heads) * half;  // (head, i) pairs that get RoPE
+  for (int idx = threadIdx.x; idx < rotated; idx += blockDim.x) {
+    const int h = idx / half;
+    const int i = idx - h * half;
+    const float angle = mul(pos, inv_freq[i]);
+    const float c = rnd<T>(cosf(angle));
+    const float s = rnd<T>(sinf(angle));
+    const float x1 = to_f32<T>(src[h * head_dim + i]);
+    const float x2 = to_f32<T>(src[h * head_dim + i + half]);
+    // first half: x1*cos + (-x2)*sin ; second half: x2*cos + x1*sin
+    const T y1 = from_f32<T>(add(rnd<T>(mul(x1, c)), rnd<T>(mul(-x2, s))));
+    const T y2 = from_f32<T>(add(rnd<T>(mul(x2, c)), rnd<T>(mul(x1, s))));
+    if (h < heads) {
+      T* dst = q_out + row * q_rs + h * q_hs;
+      dst[i] = y1;
+      dst[i + half] = y2;
+    } else if (ok) {
+      T* dst = kc + cache_row + (h - heads) * c_hs;
+      dst[i] = y1;
+      dst[i + half] = y2;
+    }
+  }
+  if (!ok) return;
+  const T* vsrc = src + (heads + kv_heads) * head_dim;
+  for (int idx = threadIdx.x; idx < kv_heads * head_dim; idx += blockDim.x) {
+    const int h = idx / head_dim;
+    const int d = idx - h * head_dim;
+    vc[cache_row + h * c_hs + d] = vsrc[idx];
+  }
+}
+
+// vllm_rlt/models/ouro.py:122-123: silu(gate) * up, each op rounded.
+template <typename T>
+__global__ void silu_mul_kernel(const T* __restrict__ gu, T* __restrict__ out, int inter,
+                                int64_t in_stride, int64_t out_stride, int64_t total) {
+  for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < total;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int64_t row = i / inter;
+    const int col = static_cast<int>(i - row * inter);
+    const float g = to_f32<T>(gu[row * in_stride + col]);
+    const float u = to_f32<T>(gu[row * in_stride + inter + col]);
+    const float s = rnd<T>(__fdiv_rn(g, add(1.f, expf(-g))));
+    out[row * out_stride + col] = from_f32<T>(mul(s, u));
+  }
+}
+
+int esize(int32_t dtype) { return dtype == RLT_F32 ? 4 : (dtype == RLT_F16 || dtype == RLT_BF16) ? 2 : 0; }
+
+}  // namespace
+}  // namespace rlt
+
+using namespace rlt;
+
+extern "C" int rlt_rms_norm(const void* x, const void* weight, const void* residual, void* out,
+                            int32_t dtype, int32_t rows, int32_t hidden, float eps,
+                            int64_t x_stride, int64_t residual_stride, int64_t out_stride,
+                            void* stream) {
+  if (esize(dtype) == 0) return RLT_E_DTYPE;
+  if (rows < 0 || hidden <= 0 || hidden > 16 * 256) return RLT_E_SHAPE;
+  if (rows == 0) return RLT_OK;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const int threads = hidden >= 2048 ? 256 : 128;
+  if (hidden > threads * 16) return RLT_E_SHAPE;
+  switch (dtype) {
+    case RLT_F32: rms_norm_kernel<float><<<rows, threads, 0, s>>>(static_cast<const float*>(x), static_cast<const float*>(weight), static_cast<const float*>(residual), static_cast<float*>(out), hidden, eps, x_stride, residual_stride, out_stride); break;
+    case RLT_F16: rms_norm_kernel<__half><<<rows, threads, 0, s>>>(static_cast<const __half*>(x), static_cast<const __half*>(weight), static_cast<const __half*>(residual), static_cast<__half*>(out), hidden, eps, x_stride, residual_stride, out_stride); break;
+    default: rms_norm_kernel<__nv_bfloat16><<<rows, threads, 0, s>>>(static_cast<const __nv_bfloat16*>(x), static_cast<const __nv_bfloat16*>(weight), static_cast<const __nv_bfloat16*>(residual), static_cast<__nv_bfloat16*>(out), hidden, eps, x_stride, residual_stride, out_stride); break;
+  }
+  return launch_status(cudaGetLastError());
+}
+
+extern "C" int rlt_rope_write_kv(const void* qkv, const int64_t* positions, const float* inv_freq,
+                                 void* q_out, void* key_cache, void* value_cache,
+                                 const int64_t* write_blocks, const int64_t* write_offsets,
+                                 int32_t* status, int32_t dtype, int32_t rows, int32_t heads,
+                                 int32_t kv_heads, int32_t head_dim, int32_t layer,
+                                 int32_t page_size, int64_t num_blocks, int64_t qkv_stride,
+                                 int64_t q_row_stride, int64_t q_head_stride,
+                                 int64_t cache_block_stride, int64_t cache_layer_stride,
+                                 int64_t cache_token_stride, int64_t cache_head_stride,
+                                 void* stream) {
+  if (esize(dtype) == 0) return RLT_E_DTYPE;
+  if (head_dim <= 0 || head_dim % 2) return RLT_E_HEAD_DIM;
+  if (heads <= 0 || kv_heads <= 0 || heads % kv_heads) return RLT_E_HEADS;
+  if (rows < 0 || layer < 0 || page_size <= 0 || num_blocks < 0) return RLT_E_SHAPE;
+  if (rows == 0) return RLT_OK;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+#define RLT_ROPE_LAUNCH(T)                                                                      \
+  rope_write_kernel<T><<<rows, 256, 0, s>>>(                                                    \
+      static_cast<const T*>(qkv), positions, inv_freq, static_cast<T*>(q_out),                  \
+      static_cast<T*>(key_cache), static_cast<T*>(value_cache), write_blocks, write_offsets,    \
+      status, heads, kv_heads, head_dim, layer, page_size, num_blocks, qkv_stride, q_row_stride, \
+      q_head_stride, cache_block_stride, cache_layer_stride, cache_token_stride,                \
+      cache_head_stride)
+  switch (dtype) {
+    case RLT_F32: RLT_ROPE_LAUNCH(float); break;
+    case RLT_F16: RLT_ROPE_LAUNCH(__half); break;
+    default: RLT_ROPE_LAUNCH(__nv_bfloat16); break;
+  }
+#undef RLT_ROPE_LAUNCH
+  return launch_status(cudaGetLastError());
+}
+
+extern "C" int rlt_silu_mul(const void* gate_up, void* out, int32_t dtype, int32_t rows,
+                            int32_t intermediate, int64_t in_stride, int64_t out_stride,
+                            void* stream) {
+  if (esize(dtype) == 0) return RLT_E_DTYPE;
+  if (rows < 0 || intermediate <= 0) return RLT_E_SHAPE;
+  if (rows == 0) return RLT_OK;
+  const int64_t total = static_cast<int64_t>(rows) * intermediate;
+  const int64_t blocks64 = (total + 255) / 256;
+  const unsigned blocks = static_cast<unsigned>(blocks64 < 8192 ? blocks64 : 8192);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  switch (dtype) {
+    case RLT_F32: silu_mul_kernel<float><<<blocks, 256, 0, s>>>(static_cast<const float*>(gate_up), static_cast<float*>(out), intermediate, in_stride, out_stride, total); break;
+    case RLT_F16: silu_mul_kernel<__half><<<blocks, 256, 0, s>>>(static_cast<const __half*>(gate_up), static_cast<__half*>(out), intermediate, in_stride, out_stride, total); break;
+    default: silu_mul_kernel<__nv_bfloat16><<<blocks, 256, 0, s>>>(static_cast<const __nv_bfloat16*>(gate_up), static_cast<__nv_bfloat16*>(out), intermediate, in_stride, out_stride, total); break;
+  }
+  return launch_status(cudaGetLastError());
+}

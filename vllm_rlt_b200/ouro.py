@@ -29,6 +29,7 @@ from dataclasses import dataclass
 import numpy as np
 import torch
 
+from .kernels import ouro_ops
 from .kernels.cache_ops import finalize, write_kv
 from .kernels.paged_attention import B200PagedAttention
 from .kernels.routing import metadata
@@ -107,8 +108,9 @@ class OuroDecoder:
     """
 
     def __init__(self, shape: OuroShape, weights: OuroWeights, capacity, device, dtype,
-                 layout: str = "last_exited", page: int = 16, seed: int = 0):
+                 layout: str = "last_exited", page: int = 16, seed: int = 0, fused: bool = True):
         self.shape, self.w = shape, weights
+        self.fused = fused  # fused sm_100a glue kernels, or the plain torch expressions
         self.device, self.dtype, self.page = torch.device(device), dtype, page
         self.layout = layout
         self.planes = shape.loops if layout == "last_exited" else 1
@@ -158,6 +160,8 @@ class OuroDecoder:
         return angles.cos().to(self.dtype).unsqueeze(1), angles.sin().to(self.dtype).unsqueeze(1)
 
     def layer(self, index, hidden, cos, sin):
+        if self.fused:
+            return self.layer_fused(index, hidden)
         s, w = self.shape, self.w
         norms = w.norms[index]
         x = rms_norm(hidden, norms[0], s.eps)
@@ -180,13 +184,35 @@ class OuroDecoder:
         mlp = (torch.nn.functional.silu(gate) * up) @ w.wdown[index].t()
         return hidden + rms_norm(mlp, norms[3], s.eps)
 
+    def layer_fused(self, index, hidden):
+        """The same layer with the glue on fused kernels: one RMSNorm kernel per
+        norm (the residual add folded into the norm that precedes it), RoPE
+        fused with the page write, one SwiGLU kernel."""
+        s, w = self.shape, self.w
+        norms = w.norms[index]
+        x = ouro_ops.rms_norm(hidden, norms[0], s.eps)
+        qkv = x @ w.wqkv[index].t()
+        q = ouro_ops.rope_write_kv(qkv, self.positions, w.inv_freq, self.key_cache,
+                                   self.value_cache, index, self.write_blocks,
+                                   self.write_offsets, s.heads, s.kv_heads, s.head_dim)
+        attn = self.attention(q, self.key_cache[:, index], self.value_cache[:, index],
+                              self.row_tables, self.lengths)
+        out = attn.reshape(hidden.shape[0], -1) @ w.wo[index].t()
+        hidden = ouro_ops.rms_norm(out, norms[1], s.eps, residual=hidden)
+        gu = ouro_ops.rms_norm(hidden, norms[2], s.eps) @ w.wgu[index].t()
+        mlp = ouro_ops.silu_mul(gu, s.intermediate) @ w.wdown[index].t()
+        return ouro_ops.rms_norm(mlp, norms[3], s.eps, residual=hidden)
+
     def core(self, hidden):
         """One recurrent pass: all layers, final norm, exit gate
         (vllm_rlt/models/ouro.py:209-217)."""
-        cos, sin = self.rope(self.positions)
+        cos, sin = (None, None) if self.fused else self.rope(self.positions)
         for index in range(self.shape.layers):
             hidden = self.layer(index, hidden, cos, sin)
-        hidden = rms_norm(hidden, self.w.final_norm, self.shape.eps)
+        if self.fused:
+            hidden = ouro_ops.rms_norm(hidden, self.w.final_norm, self.shape.eps)
+        else:
+            hidden = rms_norm(hidden, self.w.final_norm, self.shape.eps)
         gate = torch.sigmoid(hidden @ self.w.gate_w.t() + self.w.gate_b).squeeze(-1)
         return hidden, gate
 
