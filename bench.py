@@ -544,17 +544,10 @@ def run_ours(args):
     e2e_ms = e0.elapsed_time(e1)
 
     # ---- max over ranks; bytes summed over ranks
-    stats = torch.tensor([elapsed_ms, e2e_ms, float(step_bytes)], dtype=torch.float64,
-                         device=device)
-    if world > 1:
-        worst = stats[:2].clone()
-        dist.all_reduce(worst, op=dist.ReduceOp.MAX)
-        total_bytes = stats[2:].clone()
-        dist.all_reduce(total_bytes, op=dist.ReduceOp.SUM)
-        elapsed_ms, e2e_ms = worst.tolist()
-        job_bytes = total_bytes.item()
-    else:
-        job_bytes = float(step_bytes)
+    from vllm_rlt_b200.replicas import max_over_ranks
+
+    (elapsed_ms, e2e_ms), job_bytes = max_over_ranks([elapsed_ms, e2e_ms], float(step_bytes),
+                                                     device=device)
     value = job_bytes * args.steps / (elapsed_ms / 1e3) / 1e9
     e2e_value = job_bytes * args.steps / (e2e_ms / 1e3) / 1e9
     peak, peak_kind = measured_peak()
