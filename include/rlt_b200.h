@@ -122,6 +122,12 @@ int rlt_paged_prefill(const void* q, const void* key_cache, const void* value_ca
  * wheel makes the same choice internally. */
 int rlt_paged_prefill_uses_tensor_cores(int32_t dtype, int32_t head_dim, int32_t page_size);
 
+/* Diagnostics: choose the tensor-core prefill kernel for the process (2 =
+ * warp-specialised two-tile kernel, the default; 1 = single-tile kernel);
+ * returns the previous choice (any other value only queries). No counterpart
+ * in the reference. */
+int rlt_prefill_tc_select(int32_t version);
+
 /* Size of the static split-KV scratch of rlt_paged_decode_noalloc (bytes). */
 #define RLT_NOALLOC_SCRATCH_BYTES (16u << 20)
 

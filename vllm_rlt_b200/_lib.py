@@ -66,6 +66,7 @@ SIGNATURES = {
         [_p] * 8 + [_sz, _p, _i32] + [_i32] * 8 + [_i64] * 12 + [_f32, _p],
     ),
     "rlt_paged_prefill_uses_tensor_cores": (_i32, [_i32, _i32, _i32]),
+    "rlt_prefill_tc_select": (_i32, [_i32]),
     "rlt_kv_write": (_i32, [_p] * 7 + [_i32] * 6 + [_i64] * 9 + [_p]),
     "rlt_finalize": (_i32, [_p] * 5 + [_i32] * 8 + [_i64] * 4 + [_p]),
     "rlt_metadata": (_i32, [_p] * 9 + [_i32] * 7 + [_p]),

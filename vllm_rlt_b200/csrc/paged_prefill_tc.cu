@@ -21,6 +21,7 @@
 //    RLT_STATUS_TIMEOUT instead of hanging.
 #include <cudaTypedefs.h>
 
+#include <atomic>
 #include <mutex>
 
 #include "common.cuh"
@@ -86,6 +87,7 @@ struct Fmt<__nv_bfloat16> {
 
 // Warp 0: map blockIdx.x to (sequence, first query of the tile) by a running
 // prefix over ceil(qlen_s / 128). Returns seq = -1 past the last tile.
+template <int kRows = kTileM>
 __device__ void find_tile(const int32_t* cu, int num_seqs, int target, int lane, int* seq_out,
                           int* m0_out) {
   int running = 0;
@@ -94,7 +96,7 @@ __device__ void find_tile(const int32_t* cu, int num_seqs, int target, int lane,
     int tiles = 0;
     if (s < num_seqs) {
       const int qlen = cu[s + 1] - cu[s];
-      tiles = qlen > 0 ? (qlen + kTileM - 1) / kTileM : 0;
+      tiles = qlen > 0 ? (qlen + kRows - 1) / kRows : 0;
     }
     int incl = tiles;
 #pragma unroll
@@ -107,7 +109,7 @@ __device__ void find_tile(const int32_t* cu, int num_seqs, int target, int lane,
     const unsigned hit = __ballot_sync(kFullMask, mine);
     if (mine) {
       *seq_out = s;
-      *m0_out = (target - excl) * kTileM;
+      *m0_out = (target - excl) * kRows;
     }
     if (hit) return;
     running += __shfl_sync(kFullMask, incl, 31);
@@ -383,6 +385,349 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
 }
 
+
+// ---------------------------------------------------------------------------
+// Warp-specialised version: one CTA = two 128-query tiles (A, B) of one
+// sequence and head, 10 warps:
+//   warps 0-3  softmax of tile A (one query row per thread, TMEM lanes 0-127)
+//   warps 4-7  softmax of tile B
+//   warp 8     issues the tcgen05.mma (one elected thread)
+//   warp 9     issues the TMA loads (one elected thread)
+// TMEM (512 columns): S_A [0,128), S_B [128,256), O_A [256,384), O_B [384,512).
+// Shared memory: Q_A, Q_B, K, V, P_A, P_B (32 KiB each, 128-byte swizzle).
+// Hand-offs are mbarriers only. The MMA issue order per key tile t is
+//   PV_A(t), S_A(t+1), PV_B(t), S_B(t+1)
+// so the softmax of one tile runs while the tensor core works on the other.
+// K and V are single-buffered with separate release barriers: K(t+1) loads
+// once both S(t) MMAs are done, V(t+1) once both PV(t) MMAs are done.
+
+constexpr int kPairRows = 2 * kTileM;
+constexpr int kPairThreads = 320;
+constexpr uint32_t kPairTmemCols = 512;
+constexpr int kPairSmemBytes = 6 * kTileBytes + 1024;
+
+template <typename T>
+__global__ void __launch_bounds__(kPairThreads, 1)
+    paged_prefill_tc2_kernel(const __grid_constant__ PrefillTcParams p) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~static_cast<uintptr_t>(1023));
+  uint8_t* sQ[2] = {smem, smem + kTileBytes};
+  uint8_t* sK = smem + 2 * kTileBytes;
+  uint8_t* sV = smem + 3 * kTileBytes;
+  uint8_t* sP[2] = {smem + 4 * kTileBytes, smem + 5 * kTileBytes};
+
+  __shared__ __align__(8) uint64_t bar_q, bar_kfull, bar_kempty, bar_vfull, bar_vempty;
+  __shared__ __align__(8) uint64_t bar_s[2], bar_p[2], bar_pv[2];
+  __shared__ uint32_t tmem_base_sh;
+  __shared__ int tile_seq, tile_m0, abort_flag;
+
+  const int tid = threadIdx.x;
+  const int warp = tid >> 5;
+  const int lane = tid & 31;
+  const int head = blockIdx.y;
+  const int kvh = head / p.group;
+
+  if (warp == 0) find_tile<kPairRows>(p.cu, p.num_seqs, blockIdx.x, lane, &tile_seq, &tile_m0);
+  if (tid == 0) {
+    tc::mbar_init(&bar_q, 1);
+    tc::mbar_init(&bar_kfull, 1);
+    tc::mbar_init(&bar_kempty, 1);
+    tc::mbar_init(&bar_vfull, 1);
+    tc::mbar_init(&bar_vempty, 1);
+    for (int x = 0; x < 2; ++x) {
+      tc::mbar_init(&bar_s[x], 1);
+      tc::mbar_init(&bar_p[x], kTileM);
+      tc::mbar_init(&bar_pv[x], 1);
+    }
+    tc::fence_mbar_init();
+    abort_flag = 0;
+  }
+  __syncwarp();
+  if (warp == 0) tc::tmem_alloc(&tmem_base_sh, kPairTmemCols);  // warp-collective
+  tc::tc_fence_before();
+  __syncthreads();
+  tc::tc_fence_after();
+  const uint32_t tmem = tmem_base_sh;
+  volatile int* aborted = &abort_flag;  // set by any role on a timed-out wait
+
+  int seq = tile_seq;
+  const int m0 = tile_m0;
+  int qbegin = 0, qlen = 0, ctx = 0, n_tiles = 0;
+  if (seq >= 0) {
+    qbegin = p.cu[seq];
+    qlen = p.cu[seq + 1] - qbegin;
+    ctx = p.lengths[seq];
+    if (qbegin < 0 || qlen <= 0 || qbegin + qlen > p.num_tokens || ctx < 0 ||
+        static_cast<int64_t>(ctx) > static_cast<int64_t>(p.width) * p.page) {
+      if (tid == 0) raise_status(p.status, kStatusBadSequence);
+      seq = -1;
+    } else {
+      const int kmax = ctx - qlen + min(qlen - 1, m0 + kPairRows - 1);
+      n_tiles = kmax >= 0 ? kmax / kTileN + 1 : 0;
+    }
+  }
+  const bool active = seq >= 0 && n_tiles > 0;
+
+  if (active && warp == 9) {
+    // ---------------- TMA producer
+    if (lane == 0) {
+      const int pages_per_tile = kTileN / p.page;
+      auto load_pages = [&](const CUtensorMap* map, uint8_t* dst, uint64_t* bar, int t) {
+        tc::mbar_expect_tx(bar, kTileBytes);
+        for (int pg = 0; pg < pages_per_tile; ++pg) {
+          const int logical = t * pages_per_tile + pg;
+          int blk = static_cast<int>(p.num_blocks);  // out of range: zero fill
+          if (logical * p.page < ctx) {
+            const int b = p.tables[seq * p.t_rs + logical];
+            if (b >= 0 && b < p.num_blocks)
+              blk = b;
+            else
+              raise_status(p.status, kStatusBadBlock);
+          }
+#pragma unroll
+          for (int dh = 0; dh < 2; ++dh)
+            tc::tma_load_4d(dst + dh * kHalfBytes + pg * p.page * 128, map, bar, dh * 64, kvh, 0,
+                            blk);
+        }
+      };
+      tc::mbar_expect_tx(&bar_q, 2 * kTileBytes);
+      for (int x = 0; x < 2; ++x)
+        for (int dh = 0; dh < 2; ++dh)
+          tc::tma_load_3d(sQ[x] + dh * kHalfBytes, &p.qmap, &bar_q, dh * 64, head,
+                          qbegin + m0 + x * kTileM);
+      int k_issued = 0, v_issued = 0;
+      for (int t = 0; t < n_tiles && *aborted == 0; ++t) {
+        if (t > 0 && !tc::mbar_wait(&bar_kempty, (t - 1) & 1, kWaitLimit)) {
+          *aborted = 1;
+          break;
+        }
+        load_pages(&p.kmap, sK, &bar_kfull, t);
+        ++k_issued;
+        if (t > 0 && !tc::mbar_wait(&bar_vempty, (t - 1) & 1, kWaitLimit)) {
+          *aborted = 1;
+          break;
+        }
+        load_pages(&p.vmap, sV, &bar_vfull, t);
+        ++v_issued;
+      }
+      if (*aborted) {  // let issued copies land before shared memory is released
+        if (k_issued) tc::mbar_wait(&bar_kfull, (k_issued - 1) & 1, kWaitLimit);
+        if (v_issued) tc::mbar_wait(&bar_vfull, (v_issued - 1) & 1, kWaitLimit);
+        tc::mbar_wait(&bar_q, 0, kWaitLimit);
+      }
+    }
+  } else if (active && warp == 8) {
+    // ---------------- MMA issuer
+    if (lane == 0) {
+      const uint32_t idesc_qk = tc::idesc_f16(Fmt<T>::value, kTileM, kTileN, 0);
+      const uint32_t idesc_pv = tc::idesc_f16(Fmt<T>::value, kTileM, kHeadDim, 1);
+      int commits_s[2] = {0, 0}, commits_pv[2] = {0, 0}, commits_k = 0, commits_v = 0;
+      auto mma_s = [&](int x) {
+#pragma unroll
+        for (int ks = 0; ks < kHeadDim / 16; ++ks) {
+          const uint32_t off = (ks >> 2) * kHalfBytes + (ks & 3) * 32;
+          tc::mma_f16_ss(tmem + x * kTileN, tc::smem_desc_sw128(tc::smem_u32(sQ[x]) + off, 16, 1024),
+                         tc::smem_desc_sw128(tc::smem_u32(sK) + off, 16, 1024), idesc_qk, ks > 0);
+        }
+        tc::mma_commit(&bar_s[x]);
+        ++commits_s[x];
+      };
+      auto mma_pv = [&](int x, int t) {
+#pragma unroll
+        for (int ks = 0; ks < kTileN / 16; ++ks) {
+          const uint32_t aoff = (ks >> 2) * kHalfBytes + (ks & 3) * 32;
+          tc::mma_f16_ss(tmem + 2 * kTileN + x * kHeadDim,
+                         tc::smem_desc_sw128(tc::smem_u32(sP[x]) + aoff, 16, 1024),
+                         tc::smem_desc_sw128(tc::smem_u32(sV) + ks * 2048, kHalfBytes, 1024),
+                         idesc_pv, (t > 0 || ks > 0) ? 1u : 0u);
+        }
+        tc::mma_commit(&bar_pv[x]);
+        ++commits_pv[x];
+      };
+      bool ok = tc::mbar_wait(&bar_q, 0, kWaitLimit) && tc::mbar_wait(&bar_kfull, 0, kWaitLimit);
+      if (ok) {
+        tc::tc_fence_after();
+        mma_s(0);
+        mma_s(1);
+        tc::mma_commit(&bar_kempty);
+        ++commits_k;
+      }
+      for (int t = 0; ok && t < n_tiles; ++t) {
+        ok = tc::mbar_wait(&bar_p[0], t & 1, kWaitLimit) &&
+             tc::mbar_wait(&bar_vfull, t & 1, kWaitLimit);
+        if (!ok) break;
+        tc::tc_fence_after();
+        mma_pv(0, t);
+        if (t + 1 < n_tiles) {
+          ok = tc::mbar_wait(&bar_kfull, (t + 1) & 1, kWaitLimit);
+          if (!ok) break;
+          tc::tc_fence_after();
+          mma_s(0);
+        }
+        ok = tc::mbar_wait(&bar_p[1], t & 1, kWaitLimit);
+        if (!ok) break;
+        tc::tc_fence_after();
+        mma_pv(1, t);
+        tc::mma_commit(&bar_vempty);
+        ++commits_v;
+        if (t + 1 < n_tiles) {
+          mma_s(1);
+          tc::mma_commit(&bar_kempty);
+          ++commits_k;
+        }
+      }
+      if (!ok) {
+        *aborted = 1;
+        // every commit arrives once all earlier MMAs are done: wait the last
+        const int total = commits_s[0] + commits_s[1] + commits_pv[0] + commits_pv[1];
+        if (total) {
+          for (int x = 0; x < 2; ++x) {
+            if (commits_pv[x]) tc::mbar_wait(&bar_pv[x], (commits_pv[x] - 1) & 1, kWaitLimit);
+            if (commits_s[x]) tc::mbar_wait(&bar_s[x], (commits_s[x] - 1) & 1, kWaitLimit);
+          }
+        }
+        (void)commits_k;
+        (void)commits_v;
+      }
+    }
+  } else if (active && warp < 8) {
+    // ---------------- softmax of tile x, one query row per thread
+    const int x = warp >> 2;
+    const int r = tid & (kTileM - 1);
+    const uint32_t lane_base = static_cast<uint32_t>((warp & 3) * 32) << 16;
+    const uint32_t s_tmem = tmem + x * kTileN + lane_base;
+    const uint32_t o_tmem = tmem + 2 * kTileN + x * kHeadDim + lane_base;
+    const int qi = m0 + x * kTileM + r;
+    const int row_limit = min(ctx - qlen + qi, ctx - 1);
+    float m_used = -INFINITY;
+    float l_sum = 0.f;
+    int t = 0;
+    for (; t < n_tiles; ++t) {
+      // loop exits are warp-uniform: the next statement is a warp-collective
+      // tcgen05.ld
+      const bool ready = *aborted == 0 && tc::mbar_wait(&bar_s[x], t & 1, kWaitLimit);
+      if (!__all_sync(kFullMask, ready)) {
+        *aborted = 1;
+        break;
+      }
+      tc::tc_fence_after();
+      const int n0 = t * kTileN;
+      // pass 1: masked, scaled row max
+      float mx = -INFINITY;
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        uint32_t sr[32];
+        tc::tmem_ld32(s_tmem + c * 32, sr);
+        tc::tmem_ld_wait(sr);
+#pragma unroll
+        for (int j = 0; j < 32; ++j) {
+          const int key = n0 + c * 32 + j;
+          if (key <= row_limit) mx = fmaxf(mx, __uint_as_float(sr[j]) * p.scale_log2);
+        }
+      }
+      const float m_new = fmaxf(m_used, mx);
+      float factor = 1.f;
+      if (m_new > m_used + 8.f) {
+        factor = ex2(m_used - m_new);
+        m_used = m_new;
+      }
+      const float mref = m_used == -INFINITY ? 0.f : m_used;
+      // PV(t-1) must be done: it read P_x and it wrote O_x.
+      if (t > 0) {
+        if (!__all_sync(kFullMask, tc::mbar_wait(&bar_pv[x], (t - 1) & 1, kWaitLimit))) {
+          *aborted = 1;
+          break;
+        }
+        tc::tc_fence_after();
+        if (__any_sync(kFullMask, factor != 1.f)) {  // warp-collective TMEM access
+#pragma unroll
+          for (int c = 0; c < 4; ++c) {
+            uint32_t o[32];
+            tc::tmem_ld32(o_tmem + c * 32, o);
+            tc::tmem_ld_wait(o);
+#pragma unroll
+            for (int j = 0; j < 32; ++j) o[j] = __float_as_uint(__uint_as_float(o[j]) * factor);
+            tc::tmem_st32(o_tmem + c * 32, o);
+          }
+          tc::tmem_st_wait();
+        }
+      }
+      // pass 2: probabilities -> P_x (swizzled), row sum
+      float psum = 0.f;
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        uint32_t sr[32];
+        tc::tmem_ld32(s_tmem + c * 32, sr);
+        tc::tmem_ld_wait(sr);
+        uint32_t packed[16];
+#pragma unroll
+        for (int j = 0; j < 32; j += 2) {
+          const int key = n0 + c * 32 + j;
+          const float s0 = key <= row_limit ? __uint_as_float(sr[j]) * p.scale_log2 : -INFINITY;
+          const float s1 =
+              key + 1 <= row_limit ? __uint_as_float(sr[j + 1]) * p.scale_log2 : -INFINITY;
+          const float p0 = ex2(s0 - mref);
+          const float p1 = ex2(s1 - mref);
+          psum += p0 + p1;
+          packed[j / 2] = pack2<T>(p0, p1);
+        }
+        uint8_t* base = sP[x] + (c >> 1) * kHalfBytes;
+#pragma unroll
+        for (int v = 0; v < 4; ++v)
+          *reinterpret_cast<uint4*>(base + sw128(r, (c & 1) * 4 + v)) =
+              make_uint4(packed[4 * v], packed[4 * v + 1], packed[4 * v + 2], packed[4 * v + 3]);
+      }
+      l_sum = l_sum * factor + psum;
+      tc::fence_proxy_async_smem();
+      tc::tc_fence_before();
+      tc::mbar_arrive(&bar_p[x]);
+    }
+    if (t == n_tiles) {
+      if (!__all_sync(kFullMask, tc::mbar_wait(&bar_pv[x], (n_tiles - 1) & 1, kWaitLimit)))
+        *aborted = 1;
+      tc::tc_fence_after();
+    }
+    // epilogue (l_sum is in a register): warp-collective TMEM reads of O_x
+    if (!__any_sync(kFullMask, *aborted != 0)) {
+      const bool store = qi < qlen;
+      T* dst = static_cast<T*>(p.out) + (qbegin + (store ? qi : 0)) * p.o_rs + head * p.o_hs;
+      const float inv = l_sum > 0.f ? 1.f / l_sum : 0.f;
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        uint32_t o[32];
+        tc::tmem_ld32(o_tmem + c * 32, o);
+        tc::tmem_ld_wait(o);
+        if (!store) continue;
+#pragma unroll
+        for (int v = 0; v < 4; ++v) {
+          uint4 w;
+          w.x = pack2<T>(__uint_as_float(o[v * 8 + 0]) * inv, __uint_as_float(o[v * 8 + 1]) * inv);
+          w.y = pack2<T>(__uint_as_float(o[v * 8 + 2]) * inv, __uint_as_float(o[v * 8 + 3]) * inv);
+          w.z = pack2<T>(__uint_as_float(o[v * 8 + 4]) * inv, __uint_as_float(o[v * 8 + 5]) * inv);
+          w.w = pack2<T>(__uint_as_float(o[v * 8 + 6]) * inv, __uint_as_float(o[v * 8 + 7]) * inv);
+          *reinterpret_cast<uint4*>(dst + c * 32 + v * 8) = w;
+        }
+      }
+    }
+  } else if (seq >= 0 && n_tiles == 0 && warp < 8) {
+    // rows that see no keys: zeros
+    const int qi = m0 + (warp >> 2) * kTileM + (tid & (kTileM - 1));
+    if (qi < qlen) {
+      T* dst = static_cast<T*>(p.out) + (qbegin + qi) * p.o_rs + head * p.o_hs;
+      for (int c = 0; c < kHeadDim; c += 8) *reinterpret_cast<uint4*>(dst + c) = make_uint4(0, 0, 0, 0);
+    }
+  }
+  __syncthreads();
+  if (*aborted && tid == 0) raise_status(p.status, kStatusTimeout);
+  tc::tc_fence_before();
+  __syncthreads();
+  if (warp == 0) {
+    tc::tc_fence_after();
+    tc::tmem_dealloc(tmem, kPairTmemCols);
+  }
+}
+
 // ---- host side --------------------------------------------------------------
 
 PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
@@ -411,6 +756,10 @@ bool encode(CUtensorMap* map, CUtensorMapDataType type, uint32_t rank, const voi
 }
 
 bool aligned16(const void* ptr) { return (reinterpret_cast<uintptr_t>(ptr) & 15u) == 0; }
+
+// Which tensor-core kernel rlt_paged_prefill launches: 2 = warp-specialised
+// two-tile kernel (default), 1 = the single-tile kernel.
+std::atomic<int> g_prefill_version{2};
 
 }  // namespace
 
@@ -480,27 +829,50 @@ int paged_prefill_tc(const void* q, const void* key_cache, const void* value_cac
   p.o_hs = st[10];
   p.scale_log2 = scale * 1.4426950408889634f;
 
-  static std::once_flag attr_once[2];
+  static std::once_flag attr_once[4];
   const int which = dtype == RLT_BF16 ? 1 : 0;
   cudaError_t attr_err = cudaSuccess;
-  std::call_once(attr_once[which], [&] {
-    attr_err = dtype == RLT_BF16
-                   ? cudaFuncSetAttribute(paged_prefill_tc_kernel<__nv_bfloat16>,
-                                          cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes)
-                   : cudaFuncSetAttribute(paged_prefill_tc_kernel<__half>,
-                                          cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
+  const bool pair = g_prefill_version.load() == 2;
+  std::call_once(attr_once[which + (pair ? 2 : 0)], [&] {
+    if (pair)
+      attr_err = dtype == RLT_BF16
+                     ? cudaFuncSetAttribute(paged_prefill_tc2_kernel<__nv_bfloat16>,
+                                            cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                            kPairSmemBytes)
+                     : cudaFuncSetAttribute(paged_prefill_tc2_kernel<__half>,
+                                            cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                            kPairSmemBytes);
+    else
+      attr_err = dtype == RLT_BF16
+                     ? cudaFuncSetAttribute(paged_prefill_tc_kernel<__nv_bfloat16>,
+                                            cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes)
+                     : cudaFuncSetAttribute(paged_prefill_tc_kernel<__half>,
+                                            cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
   });
   if (attr_err != cudaSuccess) return static_cast<int>(attr_err);
-  const dim3 grid(static_cast<unsigned>((num_tokens + kTileM - 1) / kTileM + num_seqs), hq);
-  if (dtype == RLT_BF16)
-    paged_prefill_tc_kernel<__nv_bfloat16><<<grid, kThreads, kSmemBytes, stream>>>(p);
-  else
-    paged_prefill_tc_kernel<__half><<<grid, kThreads, kSmemBytes, stream>>>(p);
+  if (pair) {
+    const dim3 grid(static_cast<unsigned>((num_tokens + kPairRows - 1) / kPairRows + num_seqs), hq);
+    if (dtype == RLT_BF16)
+      paged_prefill_tc2_kernel<__nv_bfloat16><<<grid, kPairThreads, kPairSmemBytes, stream>>>(p);
+    else
+      paged_prefill_tc2_kernel<__half><<<grid, kPairThreads, kPairSmemBytes, stream>>>(p);
+  } else {
+    const dim3 grid(static_cast<unsigned>((num_tokens + kTileM - 1) / kTileM + num_seqs), hq);
+    if (dtype == RLT_BF16)
+      paged_prefill_tc_kernel<__nv_bfloat16><<<grid, kThreads, kSmemBytes, stream>>>(p);
+    else
+      paged_prefill_tc_kernel<__half><<<grid, kThreads, kSmemBytes, stream>>>(p);
+  }
   return launch_status(cudaGetLastError());
 }
 
 }  // namespace detail
 }  // namespace rlt
+
+extern "C" int rlt_prefill_tc_select(int32_t version) {
+  if (version != 1 && version != 2) return rlt::g_prefill_version.load();
+  return rlt::g_prefill_version.exchange(version);
+}
 
 extern "C" int rlt_paged_prefill_uses_tensor_cores(int32_t dtype, int32_t head_dim,
                                                    int32_t page_size) {
