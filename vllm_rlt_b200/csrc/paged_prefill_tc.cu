@@ -404,7 +404,8 @@ __global__ void __launch_bounds__(kThreads, 1)
 constexpr int kPairRows = 2 * kTileM;
 constexpr int kPairThreads = 320;
 constexpr uint32_t kPairTmemCols = 512;
-constexpr int kPairSmemBytes = 6 * kTileBytes + 1024;
+constexpr int kRingSlots = 3;  // K(t), V(t) stream through 3 slots: item 2t = K(t), 2t+1 = V(t)
+constexpr int kPairSmemBytes = (4 + kRingSlots) * kTileBytes + 1024;
 
 template <typename T>
 __global__ void __launch_bounds__(kPairThreads, 1)
@@ -413,11 +414,10 @@ __global__ void __launch_bounds__(kPairThreads, 1)
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~static_cast<uintptr_t>(1023));
   uint8_t* sQ[2] = {smem, smem + kTileBytes};
-  uint8_t* sK = smem + 2 * kTileBytes;
-  uint8_t* sV = smem + 3 * kTileBytes;
-  uint8_t* sP[2] = {smem + 4 * kTileBytes, smem + 5 * kTileBytes};
+  uint8_t* sP[2] = {smem + 2 * kTileBytes, smem + 3 * kTileBytes};
+  uint8_t* ring = smem + 4 * kTileBytes;  // kRingSlots x 32 KiB
 
-  __shared__ __align__(8) uint64_t bar_q, bar_kfull, bar_kempty, bar_vfull, bar_vempty;
+  __shared__ __align__(8) uint64_t bar_q, bar_full[kRingSlots], bar_empty[kRingSlots];
   __shared__ __align__(8) uint64_t bar_s[2], bar_p[2], bar_pv[2];
   __shared__ uint32_t tmem_base_sh;
   __shared__ int tile_seq, tile_m0, abort_flag;
@@ -431,10 +431,10 @@ __global__ void __launch_bounds__(kPairThreads, 1)
   if (warp == 0) find_tile<kPairRows>(p.cu, p.num_seqs, blockIdx.x, lane, &tile_seq, &tile_m0);
   if (tid == 0) {
     tc::mbar_init(&bar_q, 1);
-    tc::mbar_init(&bar_kfull, 1);
-    tc::mbar_init(&bar_kempty, 1);
-    tc::mbar_init(&bar_vfull, 1);
-    tc::mbar_init(&bar_vempty, 1);
+    for (int i = 0; i < kRingSlots; ++i) {
+      tc::mbar_init(&bar_full[i], 1);
+      tc::mbar_init(&bar_empty[i], 1);
+    }
     for (int x = 0; x < 2; ++x) {
       tc::mbar_init(&bar_s[x], 1);
       tc::mbar_init(&bar_p[x], kTileM);
@@ -496,24 +496,24 @@ __global__ void __launch_bounds__(kPairThreads, 1)
         for (int dh = 0; dh < 2; ++dh)
           tc::tma_load_3d(sQ[x] + dh * kHalfBytes, &p.qmap, &bar_q, dh * 64, head,
                           qbegin + m0 + x * kTileM);
-      int k_issued = 0, v_issued = 0;
-      for (int t = 0; t < n_tiles && *aborted == 0; ++t) {
-        if (t > 0 && !tc::mbar_wait(&bar_kempty, (t - 1) & 1, kWaitLimit)) {
+      // item i: K(i/2) when i is even, V(i/2) when odd; slot i % 3. A slot
+      // is refilled once the MMA that last read its previous item committed
+      // the slot's empty barrier.
+      const int items = 2 * n_tiles;
+      int issued = 0;
+      for (int i = 0; i < items && *aborted == 0; ++i) {
+        const int slot = i % kRingSlots;
+        if (i >= kRingSlots &&
+            !tc::mbar_wait(&bar_empty[slot], (i / kRingSlots - 1) & 1, kWaitLimit)) {
           *aborted = 1;
           break;
         }
-        load_pages(&p.kmap, sK, &bar_kfull, t);
-        ++k_issued;
-        if (t > 0 && !tc::mbar_wait(&bar_vempty, (t - 1) & 1, kWaitLimit)) {
-          *aborted = 1;
-          break;
-        }
-        load_pages(&p.vmap, sV, &bar_vfull, t);
-        ++v_issued;
+        load_pages((i & 1) ? &p.vmap : &p.kmap, ring + slot * kTileBytes, &bar_full[slot], i >> 1);
+        ++issued;
       }
       if (*aborted) {  // let issued copies land before shared memory is released
-        if (k_issued) tc::mbar_wait(&bar_kfull, (k_issued - 1) & 1, kWaitLimit);
-        if (v_issued) tc::mbar_wait(&bar_vfull, (v_issued - 1) & 1, kWaitLimit);
+        for (int i = issued - kRingSlots < 0 ? 0 : issued - kRingSlots; i < issued; ++i)
+          tc::mbar_wait(&bar_full[i % kRingSlots], (i / kRingSlots) & 1, kWaitLimit);
         tc::mbar_wait(&bar_q, 0, kWaitLimit);
       }
     }
@@ -522,73 +522,69 @@ __global__ void __launch_bounds__(kPairThreads, 1)
     if (lane == 0) {
       const uint32_t idesc_qk = tc::idesc_f16(Fmt<T>::value, kTileM, kTileN, 0);
       const uint32_t idesc_pv = tc::idesc_f16(Fmt<T>::value, kTileM, kHeadDim, 1);
-      int commits_s[2] = {0, 0}, commits_pv[2] = {0, 0}, commits_k = 0, commits_v = 0;
-      auto mma_s = [&](int x) {
+      int commits_s[2] = {0, 0}, commits_pv[2] = {0, 0};
+      auto wait_item = [&](int i) {
+        return tc::mbar_wait(&bar_full[i % kRingSlots], (i / kRingSlots) & 1, kWaitLimit);
+      };
+      auto mma_s = [&](int x, int t) {
+        const uint32_t k_addr = tc::smem_u32(ring + ((2 * t) % kRingSlots) * kTileBytes);
 #pragma unroll
         for (int ks = 0; ks < kHeadDim / 16; ++ks) {
           const uint32_t off = (ks >> 2) * kHalfBytes + (ks & 3) * 32;
           tc::mma_f16_ss(tmem + x * kTileN, tc::smem_desc_sw128(tc::smem_u32(sQ[x]) + off, 16, 1024),
-                         tc::smem_desc_sw128(tc::smem_u32(sK) + off, 16, 1024), idesc_qk, ks > 0);
+                         tc::smem_desc_sw128(k_addr + off, 16, 1024), idesc_qk, ks > 0);
         }
         tc::mma_commit(&bar_s[x]);
         ++commits_s[x];
       };
       auto mma_pv = [&](int x, int t) {
+        const uint32_t v_addr = tc::smem_u32(ring + ((2 * t + 1) % kRingSlots) * kTileBytes);
 #pragma unroll
         for (int ks = 0; ks < kTileN / 16; ++ks) {
           const uint32_t aoff = (ks >> 2) * kHalfBytes + (ks & 3) * 32;
           tc::mma_f16_ss(tmem + 2 * kTileN + x * kHeadDim,
                          tc::smem_desc_sw128(tc::smem_u32(sP[x]) + aoff, 16, 1024),
-                         tc::smem_desc_sw128(tc::smem_u32(sV) + ks * 2048, kHalfBytes, 1024),
-                         idesc_pv, (t > 0 || ks > 0) ? 1u : 0u);
+                         tc::smem_desc_sw128(v_addr + ks * 2048, kHalfBytes, 1024), idesc_pv,
+                         (t > 0 || ks > 0) ? 1u : 0u);
         }
         tc::mma_commit(&bar_pv[x]);
         ++commits_pv[x];
       };
-      bool ok = tc::mbar_wait(&bar_q, 0, kWaitLimit) && tc::mbar_wait(&bar_kfull, 0, kWaitLimit);
+      bool ok = tc::mbar_wait(&bar_q, 0, kWaitLimit) && wait_item(0);
       if (ok) {
         tc::tc_fence_after();
-        mma_s(0);
-        mma_s(1);
-        tc::mma_commit(&bar_kempty);
-        ++commits_k;
+        mma_s(0, 0);
+        mma_s(1, 0);
+        tc::mma_commit(&bar_empty[0]);  // K(0) read by both S MMAs
       }
       for (int t = 0; ok && t < n_tiles; ++t) {
-        ok = tc::mbar_wait(&bar_p[0], t & 1, kWaitLimit) &&
-             tc::mbar_wait(&bar_vfull, t & 1, kWaitLimit);
+        ok = tc::mbar_wait(&bar_p[0], t & 1, kWaitLimit) && wait_item(2 * t + 1);
         if (!ok) break;
         tc::tc_fence_after();
         mma_pv(0, t);
         if (t + 1 < n_tiles) {
-          ok = tc::mbar_wait(&bar_kfull, (t + 1) & 1, kWaitLimit);
+          ok = wait_item(2 * t + 2);
           if (!ok) break;
           tc::tc_fence_after();
-          mma_s(0);
+          mma_s(0, t + 1);
         }
         ok = tc::mbar_wait(&bar_p[1], t & 1, kWaitLimit);
         if (!ok) break;
         tc::tc_fence_after();
         mma_pv(1, t);
-        tc::mma_commit(&bar_vempty);
-        ++commits_v;
+        tc::mma_commit(&bar_empty[(2 * t + 1) % kRingSlots]);  // V(t) read by both PV MMAs
         if (t + 1 < n_tiles) {
-          mma_s(1);
-          tc::mma_commit(&bar_kempty);
-          ++commits_k;
+          mma_s(1, t + 1);
+          tc::mma_commit(&bar_empty[(2 * t + 2) % kRingSlots]);  // K(t+1) read by both S MMAs
         }
       }
       if (!ok) {
         *aborted = 1;
         // every commit arrives once all earlier MMAs are done: wait the last
-        const int total = commits_s[0] + commits_s[1] + commits_pv[0] + commits_pv[1];
-        if (total) {
-          for (int x = 0; x < 2; ++x) {
-            if (commits_pv[x]) tc::mbar_wait(&bar_pv[x], (commits_pv[x] - 1) & 1, kWaitLimit);
-            if (commits_s[x]) tc::mbar_wait(&bar_s[x], (commits_s[x] - 1) & 1, kWaitLimit);
-          }
+        for (int x = 0; x < 2; ++x) {
+          if (commits_pv[x]) tc::mbar_wait(&bar_pv[x], (commits_pv[x] - 1) & 1, kWaitLimit);
+          if (commits_s[x]) tc::mbar_wait(&bar_s[x], (commits_s[x] - 1) & 1, kWaitLimit);
         }
-        (void)commits_k;
-        (void)commits_v;
       }
     }
   } else if (active && warp < 8) {
@@ -613,26 +609,32 @@ __global__ void __launch_bounds__(kPairThreads, 1)
       }
       tc::tc_fence_after();
       const int n0 = t * kTileN;
-      // pass 1: masked, scaled row max
+      // Ten warps put three on one SM sub-partition, which caps a thread at
+      // 168 registers: S is read from TMEM twice, 64 columns per wait.
+      const bool diagonal = n0 + kTileN - 1 > row_limit;  // keys past the causal limit
       float mx = -INFINITY;
 #pragma unroll
-      for (int c = 0; c < 4; ++c) {
-        uint32_t sr[32];
-        tc::tmem_ld32(s_tmem + c * 32, sr);
-        tc::tmem_ld_wait(sr);
+      for (int hb = 0; hb < 2; ++hb) {
+        uint32_t sr[2][32];
+        tc::tmem_ld32(s_tmem + hb * 64, sr[0]);
+        tc::tmem_ld32(s_tmem + hb * 64 + 32, sr[1]);
+        tc::tmem_ld_wait(sr[0]);
+        tc::tmem_ld_wait(sr[1]);
 #pragma unroll
-        for (int j = 0; j < 32; ++j) {
-          const int key = n0 + c * 32 + j;
-          if (key <= row_limit) mx = fmaxf(mx, __uint_as_float(sr[j]) * p.scale_log2);
-        }
+        for (int c = 0; c < 2; ++c)
+#pragma unroll
+          for (int j = 0; j < 32; ++j) {
+            const float v = __uint_as_float(sr[c][j]);
+            mx = (!diagonal || n0 + hb * 64 + c * 32 + j <= row_limit) ? fmaxf(mx, v) : mx;
+          }
       }
-      const float m_new = fmaxf(m_used, mx);
+      const float m_new = fmaxf(m_used, mx * p.scale_log2);
       float factor = 1.f;
       if (m_new > m_used + 8.f) {
         factor = ex2(m_used - m_new);
         m_used = m_new;
       }
-      const float mref = m_used == -INFINITY ? 0.f : m_used;
+      const float neg_mref = m_used == -INFINITY ? 0.f : -m_used;
       // PV(t-1) must be done: it read P_x and it wrote O_x.
       if (t > 0) {
         if (!__all_sync(kFullMask, tc::mbar_wait(&bar_pv[x], (t - 1) & 1, kWaitLimit))) {
@@ -653,30 +655,36 @@ __global__ void __launch_bounds__(kPairThreads, 1)
           tc::tmem_st_wait();
         }
       }
-      // pass 2: probabilities -> P_x (swizzled), row sum
+      // probabilities p = 2^(s * scale_log2 - m) -> P_x (swizzled), row sum
       float psum = 0.f;
 #pragma unroll
-      for (int c = 0; c < 4; ++c) {
-        uint32_t sr[32];
-        tc::tmem_ld32(s_tmem + c * 32, sr);
-        tc::tmem_ld_wait(sr);
-        uint32_t packed[16];
+      for (int hb = 0; hb < 2; ++hb) {
+        uint32_t sr[2][32];
+        tc::tmem_ld32(s_tmem + hb * 64, sr[0]);
+        tc::tmem_ld32(s_tmem + hb * 64 + 32, sr[1]);
+        tc::tmem_ld_wait(sr[0]);
+        tc::tmem_ld_wait(sr[1]);
 #pragma unroll
-        for (int j = 0; j < 32; j += 2) {
-          const int key = n0 + c * 32 + j;
-          const float s0 = key <= row_limit ? __uint_as_float(sr[j]) * p.scale_log2 : -INFINITY;
-          const float s1 =
-              key + 1 <= row_limit ? __uint_as_float(sr[j + 1]) * p.scale_log2 : -INFINITY;
-          const float p0 = ex2(s0 - mref);
-          const float p1 = ex2(s1 - mref);
-          psum += p0 + p1;
-          packed[j / 2] = pack2<T>(p0, p1);
+        for (int c = 0; c < 2; ++c) {
+          uint32_t packed[16];
+#pragma unroll
+          for (int j = 0; j < 32; j += 2) {
+            const int key = n0 + hb * 64 + c * 32 + j;
+            float p0 = ex2(fmaf(__uint_as_float(sr[c][j]), p.scale_log2, neg_mref));
+            float p1 = ex2(fmaf(__uint_as_float(sr[c][j + 1]), p.scale_log2, neg_mref));
+            if (diagonal) {
+              p0 = key <= row_limit ? p0 : 0.f;
+              p1 = key + 1 <= row_limit ? p1 : 0.f;
+            }
+            psum += p0 + p1;
+            packed[j / 2] = pack2<T>(p0, p1);
+          }
+          uint8_t* base = sP[x] + hb * kHalfBytes;
+#pragma unroll
+          for (int v = 0; v < 4; ++v)
+            *reinterpret_cast<uint4*>(base + sw128(r, c * 4 + v)) =
+                make_uint4(packed[4 * v], packed[4 * v + 1], packed[4 * v + 2], packed[4 * v + 3]);
         }
-        uint8_t* base = sP[x] + (c >> 1) * kHalfBytes;
-#pragma unroll
-        for (int v = 0; v < 4; ++v)
-          *reinterpret_cast<uint4*>(base + sw128(r, (c & 1) * 4 + v)) =
-              make_uint4(packed[4 * v], packed[4 * v + 1], packed[4 * v + 2], packed[4 * v + 3]);
       }
       l_sum = l_sum * factor + psum;
       tc::fence_proxy_async_smem();
