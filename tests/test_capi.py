@@ -44,8 +44,10 @@ def test_host_only_entry_points_without_gpu():
     assert lib.rlt_version() >= 100
     # no split can be needed when every row fits one split
     assert lib.rlt_paged_decode_workspace_bytes(8, 16, 128, 16, 16) == 0
-    # graph width 4096 x page 16: up to 32 splits of fp32 (acc + max + sum)
-    assert lib.rlt_paged_decode_workspace_bytes(256, 16, 128, 16, 4096) == 256 * 32 * 16 * 130 * 4
+    # graph width 4096 x page 16: up to 128 splits of fp32 (acc + max + sum),
+    # plus one int counter per (row, query head)
+    assert lib.rlt_paged_decode_workspace_bytes(256, 16, 128, 16, 4096) == (
+        256 * 16 * 4 + 256 * 128 * 16 * 130 * 4)
     assert lib.rlt_paged_prefill_workspace_bytes(0, 16, 128, 16, 64) == 0
 
 

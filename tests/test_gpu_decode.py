@@ -123,8 +123,10 @@ def test_page_sizes_vs_oracle(page):
 
 def test_split_boundaries_and_long_rows_vs_oracle():
     """Lengths around the split chunk (256), the split alignment (32) and the
-    split cap (32 splits -> longer splits beyond 8192 tokens)."""
-    lengths = [255, 256, 257, 287, 288, 289, 511, 512, 513, 8191, 8192, 8193, 9000, 20000]
+    split cap (128 splits -> longer splits beyond 32768 tokens); the longer
+    rows finish their merge in whichever split CTA arrives last."""
+    lengths = [255, 256, 257, 287, 288, 289, 511, 512, 513, 8191, 8192, 8193, 9000, 20000,
+               32768, 32769, 40000]
     q, k, v, tables, lengths_t, out = run_case(len(lengths), 16, 16, 128, 16, "bf16", lengths,
                                                layers=1, layer=0)
     expected = oracle_rows(q, k, v, tables, lengths_t, range(len(lengths)), "bf16")

@@ -21,8 +21,10 @@
 //  * probabilities go through a per-warp shared buffer so that each lane can
 //    apply them to its own slice of the V rows it loaded;
 //  * long rows are split; each split writes an fp32 (acc, max, sum) partial
-//    and a combine kernel merges them. The split plan is a function of the
-//    row's own length only, so results are batch-invariant.
+//    and the last split CTA of a (row, head block) to finish -- counted with
+//    an atomic per (row, head block) -- merges them, so there is no separate
+//    combine launch. The split plan is a function of the row's own length
+//    only, so results are batch-invariant.
 #include "common.cuh"
 
 namespace rlt {
@@ -44,7 +46,7 @@ namespace {
 constexpr int kDecodeWarps = RLT_DECODE_WARPS;       // warps (= warp tasks) per CTA
 constexpr int kSplitAlign = 32;                      // every split starts at a multiple of this
 constexpr int kSplitChunk = RLT_DECODE_SPLIT_CHUNK;  // target tokens per split
-constexpr int kMaxSplits = 32;                       // cap; longer rows get longer splits
+constexpr int kMaxSplits = 128;                      // cap; longer rows get longer splits
 
 struct DecodeParams {
   const void* q;
@@ -56,6 +58,7 @@ struct DecodeParams {
   void* out;
   float* ws_o;   // [rows, launch_splits, hq, head_dim] unnormalised acc
   float* ws_ml;  // [rows, launch_splits, hq, 2] (running max in log2 units, sum)
+  int* counters;  // [rows, hq] finished-split counts (zeroed by the launcher)
   int32_t* status;
   int rows, hq, hkv, group, head_dim, page, width, launch_splits;
   int64_t num_blocks;
@@ -115,6 +118,45 @@ __device__ __forceinline__ int checked_length(const DecodeParams& p, int row, bo
   return ctx;
 }
 
+// Merge the split partials of one query head of one row (one warp): the
+// splits' base-2 running maxima and sums give each split's weight; the output
+// is the weighted sum of the unnormalised accumulators over the total sum.
+template <typename T>
+__device__ __forceinline__ void merge_splits(const DecodeParams& p, int row, int qh, int count,
+                                             int lane) {
+  const int64_t base = static_cast<int64_t>(row) * p.launch_splits * p.hq + qh;
+  float mx = -INFINITY;
+  for (int sp = lane; sp < count; sp += 32) mx = fmaxf(mx, p.ws_ml[(base + sp * p.hq) * 2]);
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(kFullMask, mx, o));
+  const float mref = mx == -INFINITY ? 0.f : mx;
+  float total = 0.f;
+  for (int sp = lane; sp < count; sp += 32) {
+    const float2 ml = *reinterpret_cast<const float2*>(p.ws_ml + (base + sp * p.hq) * 2);
+    total += ml.y * ex2(ml.x - mref);
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) total += __shfl_xor_sync(kFullMask, total, o);
+  const float inv = 1.f / fmaxf(total, 1e-30f);
+  T* out = static_cast<T*>(p.out) + row * p.o_rs + qh * p.o_hs;
+  for (int d4 = lane; d4 < p.head_dim / 4; d4 += 32) {
+    float4 a = make_float4(0.f, 0.f, 0.f, 0.f);
+    for (int sp = 0; sp < count; ++sp) {
+      const float w = ex2(p.ws_ml[(base + sp * p.hq) * 2] - mref);
+      const float4 v = *reinterpret_cast<const float4*>(p.ws_o + (base + sp * p.hq) * p.head_dim + d4 * 4);
+      a.x = fmaf(v.x, w, a.x);
+      a.y = fmaf(v.y, w, a.y);
+      a.z = fmaf(v.z, w, a.z);
+      a.w = fmaf(v.w, w, a.w);
+    }
+    T* dst = out + d4 * 4;
+    dst[0] = from_f32<T>(a.x * inv);
+    dst[1] = from_f32<T>(a.y * inv);
+    dst[2] = from_f32<T>(a.z * inv);
+    dst[3] = from_f32<T>(a.w * inv);
+  }
+}
+
 template <typename T, int D, int GC, bool ALIGNED>
 __global__ void __launch_bounds__(kDecodeWarps * 32, RLT_DECODE_MIN_BLOCKS)
     paged_decode_kernel(const __grid_constant__ DecodeParams p) {
@@ -138,9 +180,11 @@ __global__ void __launch_bounds__(kDecodeWarps * 32, RLT_DECODE_MIN_BLOCKS)
   const int row = blockIdx.x / blocks_per_row;
   const int task = (blockIdx.x - row * blocks_per_row) * kDecodeWarps + warp;
   const int split = blockIdx.y;
-  if (task >= tasks_per_row) return;
-  const int kvh = task / qchunks;
-  const int qh0 = kvh * p.group + (task - kvh * qchunks) * GC;
+  // Warps past the row's last task stay alive for the CTA barrier of the
+  // split merge; they compute nothing.
+  const bool active = task < tasks_per_row;
+  const int kvh = (active ? task : 0) / qchunks;
+  const int qh0 = kvh * p.group + ((active ? task : 0) - kvh * qchunks) * GC;
 
   const int g = lane / LPT;  // lane group: which token row of a warp-wide load
   const int s = lane % LPT;  // 16-byte slice of the head row
@@ -148,7 +192,7 @@ __global__ void __launch_bounds__(kDecodeWarps * 32, RLT_DECODE_MIN_BLOCKS)
 
   const int ctx = checked_length(p, row, split == 0 && task == 0 && lane == 0);
   if (ctx == 0) {
-    if (split == 0 && g == 0) {
+    if (active && split == 0 && g == 0) {
       const float zero[VEC] = {};
 #pragma unroll
       for (int c = 0; c < GC; ++c)
@@ -188,7 +232,8 @@ __global__ void __launch_bounds__(kDecodeWarps * 32, RLT_DECODE_MIN_BLOCKS)
   const bool writer = (s & ((1 << PLAIN) - 1)) == 0;
   const uint4 zero4 = make_uint4(0, 0, 0, 0);
 
-  for (int base = start; base < end; base += ITOK) {
+  const int loop_end = active ? end : start;  // idle warps skip the stream
+  for (int base = start; base < loop_end; base += ITOK) {
     const int t0 = base + g * TOK;  // first token of this lane group
     uint4 kr[TOK];
     bool page_ok = false;
@@ -363,7 +408,7 @@ __global__ void __launch_bounds__(kDecodeWarps * 32, RLT_DECODE_MIN_BLOCKS)
   }
 
   if (plan.count == 1) {
-    if (g == 0) {
+    if (active && g == 0) {
 #pragma unroll
       for (int c = 0; c < GC; ++c) {
         const float inv = 1.f / fmaxf(lsum[c], 1e-30f);
@@ -376,7 +421,7 @@ __global__ void __launch_bounds__(kDecodeWarps * 32, RLT_DECODE_MIN_BLOCKS)
     return;
   }
   const int64_t slot = (static_cast<int64_t>(row) * p.launch_splits + split) * p.hq + qh0;
-  if (g == 0) {
+  if (active && g == 0) {
 #pragma unroll
     for (int c = 0; c < GC; ++c) {
       float* dst = p.ws_o + (slot + c) * p.head_dim + s * VEC;
@@ -386,41 +431,26 @@ __global__ void __launch_bounds__(kDecodeWarps * 32, RLT_DECODE_MIN_BLOCKS)
             make_float4(acc[c][e], acc[c][e + 1], acc[c][e + 2], acc[c][e + 3]);
     }
   }
-  if (lane == 0) {
+  if (active && lane == 0) {
 #pragma unroll
     for (int c = 0; c < GC; ++c)
       *reinterpret_cast<float2*>(p.ws_ml + (slot + c) * 2) = make_float2(m[c], lsum[c]);
   }
-}
-
-// Merge the split partials of rows that needed more than one split.
-// grid = (rows, hq), block = head_dim threads (rounded up to a warp).
-template <typename T>
-__global__ void __launch_bounds__(256) decode_combine_kernel(const __grid_constant__ DecodeParams p) {
-  const int row = blockIdx.x;
-  const int qh = blockIdx.y;
-  const int ctx = checked_length(p, row, false);
-  const SplitPlan plan = split_plan(ctx, p.launch_splits);
-  if (plan.count <= 1) return;
-  const int64_t base = static_cast<int64_t>(row) * p.launch_splits * p.hq + qh;
-  float mx = -INFINITY;
-  for (int sp = 0; sp < plan.count; ++sp) mx = fmaxf(mx, p.ws_ml[(base + sp * p.hq) * 2]);
-  const float mref = mx == -INFINITY ? 0.f : mx;
-  float total = 0.f;
-  for (int sp = 0; sp < plan.count; ++sp) {
-    const float2 ml = *reinterpret_cast<const float2*>(p.ws_ml + (base + sp * p.hq) * 2);
-    total += ml.y * ex2(ml.x - mref);
+  // The last split CTA of this (row, head block) to finish merges them all
+  // (no separate combine launch). Partials are made visible before counting.
+  __threadfence();
+  __syncthreads();
+  __shared__ int merge_here;
+  if (threadIdx.x == 0) {
+    const int done = atomicAdd(p.counters + static_cast<int64_t>(row) * p.hq +
+                                   (blockIdx.x - row * blocks_per_row), 1);
+    merge_here = done == plan.count - 1;
   }
-  const float inv = 1.f / fmaxf(total, 1e-30f);
-  T* out = static_cast<T*>(p.out) + row * p.o_rs + qh * p.o_hs;
-  for (int d = threadIdx.x; d < p.head_dim; d += blockDim.x) {
-    float o = 0.f;
-    for (int sp = 0; sp < plan.count; ++sp) {
-      const float w = ex2(p.ws_ml[(base + sp * p.hq) * 2] - mref);
-      o = fmaf(p.ws_o[(base + sp * p.hq) * p.head_dim + d], w, o);
-    }
-    out[d] = from_f32<T>(o * inv);
-  }
+  __syncthreads();
+  if (!merge_here || !active) return;
+  __threadfence();
+#pragma unroll
+  for (int c = 0; c < GC; ++c) merge_splits<T>(p, row, qh0 + c, plan.count, lane);
 }
 
 // Any head_dim <= 256, any alignment: one warp per (row, query head), dims
@@ -520,9 +550,6 @@ cudaError_t launch_fast(const DecodeParams& p, cudaStream_t stream) {
     paged_decode_kernel<T, D, GC, true><<<grid, kDecodeWarps * 32, 0, stream>>>(p);
   else
     paged_decode_kernel<T, D, GC, false><<<grid, kDecodeWarps * 32, 0, stream>>>(p);
-  cudaError_t err = cudaGetLastError();
-  if (err != cudaSuccess || p.launch_splits <= 1) return err;
-  decode_combine_kernel<T><<<dim3(p.rows, p.hq), D <= 256 ? D : 256, 0, stream>>>(p);
   return cudaGetLastError();
 }
 
@@ -589,13 +616,19 @@ struct DecodeArgs {
   float scale;
 };
 
+size_t align16(size_t n) { return (n + 15) & ~static_cast<size_t>(15); }
+
+// Split scratch: [rows * hq] int counters | acc partials | (max, sum) partials.
+size_t counter_bytes(int rows, int hq) {
+  return align16(static_cast<size_t>(rows) * hq * sizeof(int));
+}
+
 size_t split_bytes(int rows, int hq, int head_dim, int page, int width) {
   const int splits = launch_splits_for(static_cast<int64_t>(page) * width);
   if (splits <= 1 || rows <= 0 || hq <= 0 || head_dim <= 0) return 0;
-  return static_cast<size_t>(rows) * splits * hq * (head_dim + 2) * sizeof(float);
+  return counter_bytes(rows, hq) +
+         static_cast<size_t>(rows) * splits * hq * (head_dim + 2) * sizeof(float);
 }
-
-size_t align16(size_t n) { return (n + 15) & ~static_cast<size_t>(15); }
 
 int validate(const DecodeArgs& a) {
   if (elem_size(a.dtype) == 0) return RLT_E_DTYPE;
@@ -650,7 +683,13 @@ DecodeParams make_params(const DecodeArgs& a, bool* fast) {
 
 int run(DecodeParams p, int32_t dtype, bool fast, void* split_ws, cudaStream_t s) {
   if (p.launch_splits > 1) {
-    p.ws_o = static_cast<float*>(split_ws);
+    // The split counters must start at zero on every call: one memset on the
+    // stream (allocation-free and capturable).
+    const size_t cbytes = counter_bytes(p.rows, p.hq);
+    const cudaError_t err = cudaMemsetAsync(split_ws, 0, cbytes, s);
+    if (err != cudaSuccess) return launch_status(err);
+    p.counters = static_cast<int*>(split_ws);
+    p.ws_o = reinterpret_cast<float*>(static_cast<char*>(split_ws) + cbytes);
     p.ws_ml = p.ws_o + static_cast<size_t>(p.rows) * p.launch_splits * p.hq * p.head_dim;
   }
   cudaError_t err;

@@ -11,10 +11,11 @@
 //
 // The array is a fixed 16 MiB per GPU that loads this part of the library and
 // stays allocated until the process exits. All calls share it and it keeps
-// the previous call's contents; nothing in it has to start at zero (every
-// split partial a call reads was written earlier in the same call). Two calls
-// that overlap on the GPU (different streams, or different host threads on
-// the same device) race on the array: serialise them.
+// the previous call's contents: each call clears the split counters it needs
+// at zero (a memset on the call's stream) and reads only split partials it
+// wrote itself. Two calls that overlap on the GPU (different streams, or
+// different host threads on the same device) race on the array: serialise
+// them.
 #include <mutex>
 
 #include "common.cuh"

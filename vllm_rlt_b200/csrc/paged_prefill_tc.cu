@@ -87,7 +87,7 @@ struct Fmt<__nv_bfloat16> {
 
 // Warp 0: map blockIdx.x to (sequence, first query of the tile) by a running
 // prefix over ceil(qlen_s / 128). Returns seq = -1 past the last tile.
-template <int kRows = kTileM>
+template <int kRows = kTileM, bool kHeavyFirst = false>
 __device__ void find_tile(const int32_t* cu, int num_seqs, int target, int lane, int* seq_out,
                           int* m0_out) {
   int running = 0;
@@ -109,7 +109,10 @@ __device__ void find_tile(const int32_t* cu, int num_seqs, int target, int lane,
     const unsigned hit = __ballot_sync(kFullMask, mine);
     if (mine) {
       *seq_out = s;
-      *m0_out = (target - excl) * kRows;
+      // Later query tiles see more keys: with kHeavyFirst a sequence's last
+      // tile is dispatched first, so long CTAs start early in the launch.
+      const int idx = kHeavyFirst ? tiles - 1 - (target - excl) : target - excl;
+      *m0_out = idx * kRows;
     }
     if (hit) return;
     running += __shfl_sync(kFullMask, incl, 31);
@@ -428,7 +431,8 @@ __global__ void __launch_bounds__(kPairThreads, 1)
   const int head = blockIdx.y;
   const int kvh = head / p.group;
 
-  if (warp == 0) find_tile<kPairRows>(p.cu, p.num_seqs, blockIdx.x, lane, &tile_seq, &tile_m0);
+  if (warp == 0)
+    find_tile<kPairRows, true>(p.cu, p.num_seqs, blockIdx.x, lane, &tile_seq, &tile_m0);
   if (tid == 0) {
     tc::mbar_init(&bar_q, 1);
     for (int i = 0; i < kRingSlots; ++i) {
