@@ -268,7 +268,7 @@ def prefill_extra(device, steps, warmup, rank):
     import vllm_rlt_b200 as rb
     from vllm_rlt_b200 import workloads
 
-    plan = workloads.config4_plan(seed=100 + rank)
+    plan = workloads.config4_plan(seed=100)  # same shape on every rank (weak scaling)
     g = torch.Generator(device=device).manual_seed(7 + rank)
     key = torch.empty((plan.num_blocks, 1, 16, 16, 128), device=device, dtype=torch.bfloat16)
     value = torch.empty_like(key)
@@ -371,7 +371,7 @@ def ouro_extra(device, steps, warmup, rank, requests=64):
     from vllm_rlt_b200.ouro import (DecodeScheduler, OuroDecoder, OuroShape, OuroWeights,
                                     decode_bytes_per_pass)
 
-    rng = np.random.default_rng(50 + rank)
+    rng = np.random.default_rng(50)  # same request mix on every rank (weak scaling)
     shape = OuroShape()
     ctx = rng.integers(256, 4097, size=requests).astype(np.int64)
     exits = rng.integers(0, 4, size=(requests, 4 * (steps + warmup) + 8))
@@ -463,8 +463,9 @@ def run_ours(args):
             print(json.dumps({"workload_line": args.workload, "n_gpus": world, **res}), flush=True)
         return
 
-    # Each rank serves its own request shard (seed = rank): weak scaling.
-    plan = workloads.config2_plan(seed=rank, rows=args.rows)
+    # Weak scaling: every rank serves a shard of the same shape (same context
+    # lengths and tables); only the synthetic K/V contents differ per rank.
+    plan = workloads.config2_plan(seed=0, rows=args.rows)
     g = torch.Generator(device=device).manual_seed(1000 + rank)
     shape = (plan.num_blocks, 1, plan.page, plan.num_kv_heads, plan.head_dim)
     kpool = torch.empty(shape, device=device, dtype=torch.bfloat16)
