@@ -50,15 +50,11 @@ def test_tensor_core_path_selection():
     assert lib.rlt_paged_prefill_uses_tensor_cores(_lib.BF16, 128, 5) == 0
 
 
-@pytest.mark.parametrize("dtype", ["bf16", "f16"])
-def test_chunked_prefill_with_prefix_reuse_vs_oracle(dtype):
-    """Config-4-shaped (scaled down): several sequences, chunk after a reused
-    prefix, fragmented tables, GQA 1, head_dim 128."""
-    rng = np.random.default_rng(7)
-    page, hkv, d = 16, 4, 128
-    prompt = [300, 517, 64, 1000]
-    prefix = [0, 256, 17, 640]
-    chunk = [min(200, p - s) for p, s in zip(prompt, prefix)]
+def _prefix_reuse_case(dtype, page=16, hkv=4, seed=7, prompt=(300, 517, 64, 1000),
+                       prefix=(0, 256, 17, 640), chunk_cap=200):
+    rng = np.random.default_rng(seed)
+    d = 128
+    chunk = [min(chunk_cap, p - s) for p, s in zip(prompt, prefix)]
     lengths = [s + c for s, c in zip(prefix, chunk)]
     width = max(math.ceil(n / page) for n in lengths)
     num_blocks = sum(math.ceil(n / page) for n in lengths) + 3
@@ -80,4 +76,47 @@ def test_chunked_prefill_with_prefix_reuse_vs_oracle(dtype):
                            torch.from_numpy(cu).cuda(), max(chunk))
     expected = oracle.paged_prefill(to_numpy(q), to_numpy(key[:, 0]), to_numpy(value[:, 0]),
                                     tables, np.array(lengths), cu, dtype)
+    return out, expected
+
+
+@pytest.mark.parametrize("dtype", ["bf16", "f16"])
+def test_chunked_prefill_with_prefix_reuse_vs_oracle(dtype):
+    """Config-4-shaped (scaled down): several sequences, chunk after a reused
+    prefix, fragmented tables, GQA 1, head_dim 128."""
+    out, expected = _prefix_reuse_case(dtype)
     assert_close(to_numpy(out), expected, dtype)
+
+
+# The reference's own bound for its tensor-core prefill (FA4, which rounds P
+# to the input dtype before the PV product) against the fp32 torch path:
+# tests/test_flash_attention.py:66-67 and :187-188.
+FA4_TOLERANCE = {"bf16": dict(atol=0.015, rtol=0.02, ulps=0),
+                 "f16": dict(atol=0.002, rtol=0.02, ulps=0)}
+
+
+def _with_version(version, fn):
+    lib = _lib.load()
+    previous = lib.rlt_prefill_tc_select(version)
+    try:
+        result = fn()
+        torch.cuda.synchronize()
+    finally:
+        lib.rlt_prefill_tc_select(previous)
+    return result
+
+
+@pytest.mark.parametrize("page", [16, 64])
+@pytest.mark.parametrize("dtype", ["bf16", "f16"])
+def test_each_tensor_core_kernel_vs_oracle(dtype, page):
+    """Every tensor-core prefill kernel (1: single tile; 2: two tiles, P in
+    shared memory; 3: two tiles, P in TMEM) on long chunks that run many key
+    tiles, with ragged tails and a chunk shorter than one tile. Kernels 2 and
+    3 differ only in where P is held, so their outputs are bit-identical."""
+    case = dict(page=page, seed=11, prompt=(1500, 2100, 90, 777), prefix=(0, 700, 30, 1),
+                chunk_cap=1100)
+    outs = {}
+    for version in (1, 2, 3):
+        out, expected = _with_version(version, lambda: _prefix_reuse_case(dtype, **case))
+        assert_close(to_numpy(out), expected, dtype, **FA4_TOLERANCE[dtype])
+        outs[version] = out
+    assert torch.equal(outs[2], outs[3])

@@ -74,6 +74,63 @@ __device__ __forceinline__ uint32_t pack2<__half>(float lo, float hi) {
   return *reinterpret_cast<uint32_t*>(&v);
 }
 
+
+// ---- softmax arithmetic helpers (sm_100 packed fp32x2 and 3-input max) ----
+
+__device__ __forceinline__ uint64_t pk2(float lo, float hi) {
+  uint64_t r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(lo), "f"(hi));
+  return r;
+}
+__device__ __forceinline__ void upk2(uint64_t v, float& lo, float& hi) {
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(lo), "=f"(hi) : "l"(v));
+}
+__device__ __forceinline__ uint64_t fma2(uint64_t a, uint64_t b, uint64_t c) {
+  uint64_t r;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(r) : "l"(a), "l"(b), "l"(c));
+  return r;
+}
+__device__ __forceinline__ uint64_t add2(uint64_t a, uint64_t b) {
+  uint64_t r;
+  asm("add.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+  return r;
+}
+__device__ __forceinline__ float max3(float a, float b, float c) {
+  float r;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(r) : "f"(a), "f"(b), "f"(c));
+  return r;
+}
+
+// 2^x for two lanes without the XU unit (which executes MUFU ex2 and also
+// every float<->int conversion and rounding instruction): x is clamped to
+// [-126, +inf), rounded to the nearest integer i by adding 1.5 * 2^23 (the
+// sum's low mantissa bits then hold i), f = x - i lies in [-1/2, 1/2], and
+// 2^f ~= 1 + f (c1 + f (c2 + f c3)) -- a cubic fitted here to the relative
+// error of 2^f on [-1/2, 1/2] by iteratively reweighted least squares
+// (Lawson), max relative error 1.0e-4, far below the bf16/fp16 rounding of
+// P. 2^i is added to the exponent field with integer arithmetic.
+__device__ __forceinline__ uint64_t exp2_poly2(uint64_t x2) {
+  constexpr float c1 = 0.693282902f, c2 = 0.242210627f, c3 = 0.0550086908f;
+  constexpr float kMagic = 12582912.0f;  // 1.5 * 2^23
+  float x0, x1;
+  upk2(x2, x0, x1);
+  const uint64_t x = pk2(fmaxf(x0, -126.f), fmaxf(x1, -126.f));
+  const uint64_t t = add2(x, pk2(kMagic, kMagic));  // round to nearest integer
+  const uint64_t r = add2(t, pk2(-kMagic, -kMagic));
+  const uint64_t f = fma2(r, pk2(-1.f, -1.f), x);   // x - round(x)
+  uint64_t q = fma2(pk2(c3, c3), f, pk2(c2, c2));
+  q = fma2(q, f, pk2(c1, c1));
+  q = fma2(q, f, pk2(1.f, 1.f));
+  float q0, q1, t0, t1;
+  upk2(q, q0, q1);
+  upk2(t, t0, t1);
+  // exponent += i, with i = bits(t) - bits(kMagic)
+  const uint32_t bias = __float_as_uint(kMagic) << 23;
+  q0 = __uint_as_float(__float_as_uint(q0) + (__float_as_uint(t0) << 23) - bias);
+  q1 = __uint_as_float(__float_as_uint(q1) + (__float_as_uint(t1) << 23) - bias);
+  return pk2(q0, q1);
+}
+
 template <typename T>
 struct Fmt;
 template <>
@@ -407,20 +464,31 @@ __global__ void __launch_bounds__(kThreads, 1)
 constexpr int kPairRows = 2 * kTileM;
 constexpr int kPairThreads = 320;
 constexpr uint32_t kPairTmemCols = 512;
-constexpr int kRingSlots = 3;  // K(t), V(t) stream through 3 slots: item 2t = K(t), 2t+1 = V(t)
-constexpr int kPairSmemBytes = (4 + kRingSlots) * kTileBytes + 1024;
+// K(t), V(t) stream through a ring of 32 KiB slots: item 2t = K(t), 2t+1 =
+// V(t), slot = item % slots. With P in TMEM (kPTmem) the two P buffers of
+// shared memory go to the ring instead: 5 slots rather than 3.
+template <bool kPTmem>
+struct PairLayout {
+  static constexpr int kSlots = kPTmem ? 5 : 3;
+  static constexpr int kPBuffers = kPTmem ? 0 : 2;
+  static constexpr int kSmemBytes = (2 + kPBuffers + kSlots) * kTileBytes + 1024;
+};
+constexpr int kMaxRingSlots = 5;
+static_assert(PairLayout<true>::kSmemBytes <= 227 * 1024 && PairLayout<false>::kSmemBytes <= 227 * 1024,
+              "shared memory per CTA");
 
-template <typename T>
+template <typename T, bool kPTmem>
 __global__ void __launch_bounds__(kPairThreads, 1)
     paged_prefill_tc2_kernel(const __grid_constant__ PrefillTcParams p) {
+  constexpr int kRingSlots = PairLayout<kPTmem>::kSlots;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~static_cast<uintptr_t>(1023));
   uint8_t* sQ[2] = {smem, smem + kTileBytes};
-  uint8_t* sP[2] = {smem + 2 * kTileBytes, smem + 3 * kTileBytes};
-  uint8_t* ring = smem + 4 * kTileBytes;  // kRingSlots x 32 KiB
+  // P_x (shared-memory variant only) at smem + (2 + x) * kTileBytes
+  uint8_t* ring = smem + (2 + PairLayout<kPTmem>::kPBuffers) * kTileBytes;
 
-  __shared__ __align__(8) uint64_t bar_q, bar_full[kRingSlots], bar_empty[kRingSlots];
+  __shared__ __align__(8) uint64_t bar_q, bar_full[kMaxRingSlots], bar_empty[kMaxRingSlots];
   __shared__ __align__(8) uint64_t bar_s[2], bar_p[2], bar_pv[2];
   __shared__ uint32_t tmem_base_sh;
   __shared__ int tile_seq, tile_m0, abort_flag;
@@ -545,11 +613,19 @@ __global__ void __launch_bounds__(kPairThreads, 1)
         const uint32_t v_addr = tc::smem_u32(ring + ((2 * t + 1) % kRingSlots) * kTileBytes);
 #pragma unroll
         for (int ks = 0; ks < kTileN / 16; ++ks) {
-          const uint32_t aoff = (ks >> 2) * kHalfBytes + (ks & 3) * 32;
-          tc::mma_f16_ss(tmem + 2 * kTileN + x * kHeadDim,
-                         tc::smem_desc_sw128(tc::smem_u32(sP[x]) + aoff, 16, 1024),
-                         tc::smem_desc_sw128(v_addr + ks * 2048, kHalfBytes, 1024), idesc_pv,
-                         (t > 0 || ks > 0) ? 1u : 0u);
+          const uint64_t bdesc = tc::smem_desc_sw128(v_addr + ks * 2048, kHalfBytes, 1024);
+          const uint32_t acc = (t > 0 || ks > 0) ? 1u : 0u;
+          if constexpr (kPTmem) {
+            // P_x over the first 64 columns of S_x: 8 columns (16 keys) per step
+            tc::mma_f16_ts(tmem + 2 * kTileN + x * kHeadDim, tmem + x * kTileN + ks * 8, bdesc,
+                           idesc_pv, acc);
+          } else {
+            const uint32_t aoff = (ks >> 2) * kHalfBytes + (ks & 3) * 32;
+            tc::mma_f16_ss(tmem + 2 * kTileN + x * kHeadDim,
+                           tc::smem_desc_sw128(tc::smem_u32(smem + (2 + x) * kTileBytes) + aoff,
+                                               16, 1024),
+                           bdesc, idesc_pv, acc);
+          }
         }
         tc::mma_commit(&bar_pv[x]);
         ++commits_pv[x];
@@ -615,7 +691,9 @@ __global__ void __launch_bounds__(kPairThreads, 1)
       const int n0 = t * kTileN;
       // Ten warps put three on one SM sub-partition, which caps a thread at
       // 168 registers: S is read from TMEM twice, 64 columns per wait.
-      const bool diagonal = n0 + kTileN - 1 > row_limit;  // keys past the causal limit
+      // keys past the causal limit somewhere in the warp (warp-uniform, so the
+      // TMEM collectives below never sit under a divergent branch)
+      const bool diagonal = __any_sync(kFullMask, n0 + kTileN - 1 > row_limit);
       float mx = -INFINITY;
 #pragma unroll
       for (int hb = 0; hb < 2; ++hb) {
@@ -624,13 +702,18 @@ __global__ void __launch_bounds__(kPairThreads, 1)
         tc::tmem_ld32(s_tmem + hb * 64 + 32, sr[1]);
         tc::tmem_ld_wait(sr[0]);
         tc::tmem_ld_wait(sr[1]);
+        if (diagonal) {
+#pragma unroll
+          for (int c = 0; c < 2; ++c)
+#pragma unroll
+            for (int j = 0; j < 32; ++j)
+              if (n0 + hb * 64 + c * 32 + j > row_limit) sr[c][j] = __float_as_uint(-INFINITY);
+        }
 #pragma unroll
         for (int c = 0; c < 2; ++c)
 #pragma unroll
-          for (int j = 0; j < 32; ++j) {
-            const float v = __uint_as_float(sr[c][j]);
-            mx = (!diagonal || n0 + hb * 64 + c * 32 + j <= row_limit) ? fmaxf(mx, v) : mx;
-          }
+          for (int j = 0; j < 32; j += 2)
+            mx = max3(mx, __uint_as_float(sr[c][j]), __uint_as_float(sr[c][j + 1]));
       }
       const float m_new = fmaxf(m_used, mx * p.scale_log2);
       float factor = 1.f;
@@ -659,39 +742,58 @@ __global__ void __launch_bounds__(kPairThreads, 1)
           tc::tmem_st_wait();
         }
       }
-      // probabilities p = 2^(s * scale_log2 - m) -> P_x (swizzled), row sum
-      float psum = 0.f;
+      // probabilities p = 2^(s * scale_log2 - m) -> P_x (swizzled), row sum.
+      // Half of the column pairs take ex2 on the MUFU unit, the other half
+      // the FMA-pipe polynomial; arguments and sums use packed fp32x2 ops.
+      uint64_t psum2 = pk2(0.f, 0.f);
+      const uint64_t scale2 = pk2(p.scale_log2, p.scale_log2);
+      const uint64_t neg2 = pk2(neg_mref, neg_mref);
 #pragma unroll
-      for (int hb = 0; hb < 2; ++hb) {
-        uint32_t sr[2][32];
-        tc::tmem_ld32(s_tmem + hb * 64, sr[0]);
-        tc::tmem_ld32(s_tmem + hb * 64 + 32, sr[1]);
-        tc::tmem_ld_wait(sr[0]);
-        tc::tmem_ld_wait(sr[1]);
+      for (int cc = 0; cc < 4; ++cc) {  // one 32-column chunk per TMEM wait: fewer live registers
+        uint32_t sr[32];
+        tc::tmem_ld32(s_tmem + cc * 32, sr);
+        tc::tmem_ld_wait(sr);
+        uint32_t packed[16];
 #pragma unroll
-        for (int c = 0; c < 2; ++c) {
-          uint32_t packed[16];
-#pragma unroll
-          for (int j = 0; j < 32; j += 2) {
-            const int key = n0 + hb * 64 + c * 32 + j;
-            float p0 = ex2(fmaf(__uint_as_float(sr[c][j]), p.scale_log2, neg_mref));
-            float p1 = ex2(fmaf(__uint_as_float(sr[c][j + 1]), p.scale_log2, neg_mref));
-            if (diagonal) {
-              p0 = key <= row_limit ? p0 : 0.f;
-              p1 = key + 1 <= row_limit ? p1 : 0.f;
-            }
-            psum += p0 + p1;
-            packed[j / 2] = pack2<T>(p0, p1);
+        for (int j = 0; j < 32; j += 2) {
+          const uint64_t arg =
+              fma2(pk2(__uint_as_float(sr[j]), __uint_as_float(sr[j + 1])), scale2, neg2);
+          float p0, p1;
+          if ((j & 2) == 0) {
+            float a0, a1;
+            upk2(arg, a0, a1);
+            p0 = ex2(a0);
+            p1 = ex2(a1);
+          } else {
+            upk2(exp2_poly2(arg), p0, p1);
           }
-          uint8_t* base = sP[x] + hb * kHalfBytes;
+          if (diagonal) {
+            const int key = n0 + cc * 32 + j;
+            p0 = key <= row_limit ? p0 : 0.f;
+            p1 = key + 1 <= row_limit ? p1 : 0.f;
+          }
+          psum2 = add2(psum2, pk2(p0, p1));
+          packed[j / 2] = pack2<T>(p0, p1);
+        }
+        if constexpr (kPTmem) {
+          // P columns [16 cc, 16 cc + 16) of S_x: S columns this thread already read
+          tc::tmem_st16(s_tmem + cc * 16, packed);
+        } else {
+          uint8_t* base = smem + (2 + x) * kTileBytes + (cc >> 1) * kHalfBytes;  // P_x
 #pragma unroll
           for (int v = 0; v < 4; ++v)
-            *reinterpret_cast<uint4*>(base + sw128(r, c * 4 + v)) =
+            *reinterpret_cast<uint4*>(base + sw128(r, (cc & 1) * 4 + v)) =
                 make_uint4(packed[4 * v], packed[4 * v + 1], packed[4 * v + 2], packed[4 * v + 3]);
         }
       }
+      float psum_lo, psum_hi;
+      upk2(psum2, psum_lo, psum_hi);
+      const float psum = psum_lo + psum_hi;
       l_sum = l_sum * factor + psum;
-      tc::fence_proxy_async_smem();
+      if constexpr (kPTmem)
+        tc::tmem_st_wait();
+      else
+        tc::fence_proxy_async_smem();
       tc::tc_fence_before();
       tc::mbar_arrive(&bar_p[x]);
     }
@@ -769,9 +871,24 @@ bool encode(CUtensorMap* map, CUtensorMapDataType type, uint32_t rank, const voi
 
 bool aligned16(const void* ptr) { return (reinterpret_cast<uintptr_t>(ptr) & 15u) == 0; }
 
-// Which tensor-core kernel rlt_paged_prefill launches: 2 = warp-specialised
-// two-tile kernel (default), 1 = the single-tile kernel.
-std::atomic<int> g_prefill_version{2};
+// Which tensor-core kernel rlt_paged_prefill launches: 3 = warp-specialised
+// two-tile kernel with P in TMEM (default), 2 = the same with P in shared
+// memory, 1 = the single-tile kernel.
+std::atomic<int> g_prefill_version{3};
+
+template <typename T, bool kPTmem>
+cudaError_t launch_pair(dim3 grid, const PrefillTcParams& p, cudaStream_t stream) {
+  constexpr int bytes = PairLayout<kPTmem>::kSmemBytes;
+  static std::once_flag once;
+  static cudaError_t attr_err = cudaSuccess;
+  std::call_once(once, [] {
+    attr_err = cudaFuncSetAttribute(paged_prefill_tc2_kernel<T, kPTmem>,
+                                    cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+  });
+  if (attr_err != cudaSuccess) return attr_err;
+  paged_prefill_tc2_kernel<T, kPTmem><<<grid, kPairThreads, bytes, stream>>>(p);
+  return cudaSuccess;
+}
 
 }  // namespace
 
@@ -841,40 +958,34 @@ int paged_prefill_tc(const void* q, const void* key_cache, const void* value_cac
   p.o_hs = st[10];
   p.scale_log2 = scale * 1.4426950408889634f;
 
-  static std::once_flag attr_once[4];
-  const int which = dtype == RLT_BF16 ? 1 : 0;
-  cudaError_t attr_err = cudaSuccess;
-  const bool pair = g_prefill_version.load() == 2;
-  std::call_once(attr_once[which + (pair ? 2 : 0)], [&] {
-    if (pair)
-      attr_err = dtype == RLT_BF16
-                     ? cudaFuncSetAttribute(paged_prefill_tc2_kernel<__nv_bfloat16>,
-                                            cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                            kPairSmemBytes)
-                     : cudaFuncSetAttribute(paged_prefill_tc2_kernel<__half>,
-                                            cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                            kPairSmemBytes);
-    else
+  const int version = g_prefill_version.load();
+  if (version == 1) {
+    static std::once_flag attr_once[2];
+    cudaError_t attr_err = cudaSuccess;
+    std::call_once(attr_once[dtype == RLT_BF16 ? 1 : 0], [&] {
       attr_err = dtype == RLT_BF16
                      ? cudaFuncSetAttribute(paged_prefill_tc_kernel<__nv_bfloat16>,
                                             cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes)
                      : cudaFuncSetAttribute(paged_prefill_tc_kernel<__half>,
                                             cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
-  });
-  if (attr_err != cudaSuccess) return static_cast<int>(attr_err);
-  if (pair) {
-    const dim3 grid(static_cast<unsigned>((num_tokens + kPairRows - 1) / kPairRows + num_seqs), hq);
-    if (dtype == RLT_BF16)
-      paged_prefill_tc2_kernel<__nv_bfloat16><<<grid, kPairThreads, kPairSmemBytes, stream>>>(p);
-    else
-      paged_prefill_tc2_kernel<__half><<<grid, kPairThreads, kPairSmemBytes, stream>>>(p);
-  } else {
+    });
+    if (attr_err != cudaSuccess) return static_cast<int>(attr_err);
     const dim3 grid(static_cast<unsigned>((num_tokens + kTileM - 1) / kTileM + num_seqs), hq);
     if (dtype == RLT_BF16)
       paged_prefill_tc_kernel<__nv_bfloat16><<<grid, kThreads, kSmemBytes, stream>>>(p);
     else
       paged_prefill_tc_kernel<__half><<<grid, kThreads, kSmemBytes, stream>>>(p);
+    return launch_status(cudaGetLastError());
   }
+  const dim3 grid(static_cast<unsigned>((num_tokens + kPairRows - 1) / kPairRows + num_seqs), hq);
+  cudaError_t err;
+  if (version == 2)
+    err = dtype == RLT_BF16 ? launch_pair<__nv_bfloat16, false>(grid, p, stream)
+                            : launch_pair<__half, false>(grid, p, stream);
+  else
+    err = dtype == RLT_BF16 ? launch_pair<__nv_bfloat16, true>(grid, p, stream)
+                            : launch_pair<__half, true>(grid, p, stream);
+  if (err != cudaSuccess) return static_cast<int>(err);
   return launch_status(cudaGetLastError());
 }
 
@@ -882,7 +993,7 @@ int paged_prefill_tc(const void* q, const void* key_cache, const void* value_cac
 }  // namespace rlt
 
 extern "C" int rlt_prefill_tc_select(int32_t version) {
-  if (version != 1 && version != 2) return rlt::g_prefill_version.load();
+  if (version < 1 || version > 3) return rlt::g_prefill_version.load();
   return rlt::g_prefill_version.exchange(version);
 }
 
