@@ -542,121 +542,181 @@ __global__ void __launch_bounds__(kPairThreads, 1)
   const bool active = seq >= 0 && n_tiles > 0;
 
   if (active && warp == 9) {
-    // ---------------- TMA producer
+    // ---------------- TMA producer. The warp's lanes fetch the block ids of
+    // a key tile together (lane j: page j) one tile ahead of its copies, so
+    // no table read sits between two copies; lane 0 issues the copies.
+    const int pages_per_tile = kTileN / p.page;
+    auto tile_pages = [&](int t) {
+      int blk = static_cast<int>(p.num_blocks);  // out of range: zero fill
+      const int logical = t * pages_per_tile + lane;
+      if (lane < pages_per_tile && t < n_tiles && logical * p.page < ctx) {
+        const int b = p.tables[seq * p.t_rs + logical];
+        if (b >= 0 && b < p.num_blocks)
+          blk = b;
+        else
+          raise_status(p.status, kStatusBadBlock);
+      }
+      return blk;
+    };
+    int cur = tile_pages(0);
+    int nxt = tile_pages(1);
     if (lane == 0) {
-      const int pages_per_tile = kTileN / p.page;
-      auto load_pages = [&](const CUtensorMap* map, uint8_t* dst, uint64_t* bar, int t) {
-        tc::mbar_expect_tx(bar, kTileBytes);
-        for (int pg = 0; pg < pages_per_tile; ++pg) {
-          const int logical = t * pages_per_tile + pg;
-          int blk = static_cast<int>(p.num_blocks);  // out of range: zero fill
-          if (logical * p.page < ctx) {
-            const int b = p.tables[seq * p.t_rs + logical];
-            if (b >= 0 && b < p.num_blocks)
-              blk = b;
-            else
-              raise_status(p.status, kStatusBadBlock);
-          }
-#pragma unroll
-          for (int dh = 0; dh < 2; ++dh)
-            tc::tma_load_4d(dst + dh * kHalfBytes + pg * p.page * 128, map, bar, dh * 64, kvh, 0,
-                            blk);
-        }
-      };
       tc::mbar_expect_tx(&bar_q, 2 * kTileBytes);
       for (int x = 0; x < 2; ++x)
         for (int dh = 0; dh < 2; ++dh)
           tc::tma_load_3d(sQ[x] + dh * kHalfBytes, &p.qmap, &bar_q, dh * 64, head,
                           qbegin + m0 + x * kTileM);
-      // item i: K(i/2) when i is even, V(i/2) when odd; slot i % 3. A slot
-      // is refilled once the MMA that last read its previous item committed
-      // the slot's empty barrier.
-      const int items = 2 * n_tiles;
-      int issued = 0;
-      for (int i = 0; i < items && *aborted == 0; ++i) {
-        const int slot = i % kRingSlots;
-        if (i >= kRingSlots &&
-            !tc::mbar_wait(&bar_empty[slot], (i / kRingSlots - 1) & 1, kWaitLimit)) {
-          *aborted = 1;
-          break;
-        }
-        load_pages((i & 1) ? &p.vmap : &p.kmap, ring + slot * kTileBytes, &bar_full[slot], i >> 1);
-        ++issued;
+    }
+    // item i: K(i/2) when i is even, V(i/2) when odd; slot i % slots. A slot
+    // is refilled once the MMA that last read its previous item committed
+    // the slot's empty barrier.
+    const int items = 2 * n_tiles;
+    int issued = 0;
+    bool stop = false;
+    for (int i = 0; i < items; ++i) {
+      const int slot = i % kRingSlots;
+      int ok = 1;
+      if (lane == 0)
+        ok = *aborted == 0 &&
+             (i < kRingSlots ||
+              tc::mbar_wait(&bar_empty[slot], (i / kRingSlots - 1) & 1, kWaitLimit));
+      if (!__shfl_sync(kFullMask, ok, 0)) {
+        stop = true;
+        break;
       }
-      if (*aborted) {  // let issued copies land before shared memory is released
-        for (int i = issued - kRingSlots < 0 ? 0 : issued - kRingSlots; i < issued; ++i)
-          tc::mbar_wait(&bar_full[i % kRingSlots], (i / kRingSlots) & 1, kWaitLimit);
-        tc::mbar_wait(&bar_q, 0, kWaitLimit);
+      uint8_t* dst = ring + slot * kTileBytes;
+      const CUtensorMap* map = (i & 1) ? &p.vmap : &p.kmap;
+      if (lane == 0) tc::mbar_expect_tx(&bar_full[slot], kTileBytes);
+      __syncwarp();
+      if (lane < pages_per_tile) {  // lane j copies page j of the tile
+#pragma unroll
+        for (int dh = 0; dh < 2; ++dh)
+          tc::tma_load_4d(dst + dh * kHalfBytes + lane * p.page * 128, map, &bar_full[slot],
+                          dh * 64, kvh, 0, cur);
       }
+      ++issued;
+      if (i & 1) {
+        cur = nxt;
+        nxt = tile_pages((i >> 1) + 2);
+      }
+    }
+    if (lane == 0 && (stop || *aborted)) {  // let issued copies land before shared memory goes
+      *aborted = 1;
+      for (int i = issued - kRingSlots < 0 ? 0 : issued - kRingSlots; i < issued; ++i)
+        tc::mbar_wait(&bar_full[i % kRingSlots], (i / kRingSlots) & 1, kWaitLimit);
+      tc::mbar_wait(&bar_q, 0, kWaitLimit);
     }
   } else if (active && warp == 8) {
     // ---------------- MMA issuer
     if (lane == 0) {
-      const uint32_t idesc_qk = tc::idesc_f16(Fmt<T>::value, kTileM, kTileN, 0);
-      const uint32_t idesc_pv = tc::idesc_f16(Fmt<T>::value, kTileM, kHeadDim, 1);
+      constexpr uint32_t idesc_qk = tc::idesc_f16(Fmt<T>::value, kTileM, kTileN, 0);
+      constexpr uint32_t idesc_pv = tc::idesc_f16(Fmt<T>::value, kTileM, kHeadDim, 1);
+      // Descriptor words computed once; a k-step, a query tile or a ring slot
+      // moves the start address only, a 32-bit add on the low word. Building
+      // descriptors per MMA made this single thread, not the tensor core, the
+      // limit on the MMA rate.
+      constexpr uint32_t kTileStep = kTileBytes >> 4;
+      const uint64_t q_desc = tc::smem_desc_sw128(tc::smem_u32(smem), 16, 1024);  // Q_A, Q_B, P_A, P_B
+      const uint64_t k_desc = tc::smem_desc_sw128(tc::smem_u32(ring), 16, 1024);
+      const uint64_t v_desc = tc::smem_desc_sw128(tc::smem_u32(ring), kHalfBytes, 1024);
+      const uint32_t q_lo = static_cast<uint32_t>(q_desc), q_hi = static_cast<uint32_t>(q_desc >> 32);
+      const uint32_t k_lo = static_cast<uint32_t>(k_desc), k_hi = static_cast<uint32_t>(k_desc >> 32);
+      const uint32_t v_lo = static_cast<uint32_t>(v_desc), v_hi = static_cast<uint32_t>(v_desc >> 32);
       int commits_s[2] = {0, 0}, commits_pv[2] = {0, 0};
       auto wait_item = [&](int i) {
         return tc::mbar_wait(&bar_full[i % kRingSlots], (i / kRingSlots) & 1, kWaitLimit);
       };
-      auto mma_s = [&](int x, int t) {
-        const uint32_t k_addr = tc::smem_u32(ring + ((2 * t) % kRingSlots) * kTileBytes);
+      // k-steps [k0, k1) of S_x = Q_x K^T, K in ring slot `slot`
+      auto s_steps = [&](int x, int slot, int k0, int k1) {
+        const uint32_t qb = q_lo + x * kTileStep;
+        const uint32_t kb = k_lo + slot * kTileStep;
 #pragma unroll
-        for (int ks = 0; ks < kHeadDim / 16; ++ks) {
-          const uint32_t off = (ks >> 2) * kHalfBytes + (ks & 3) * 32;
-          tc::mma_f16_ss(tmem + x * kTileN, tc::smem_desc_sw128(tc::smem_u32(sQ[x]) + off, 16, 1024),
-                         tc::smem_desc_sw128(k_addr + off, 16, 1024), idesc_qk, ks > 0);
+        for (int ks = k0; ks < k1; ++ks) {
+          const uint32_t off = ((ks >> 2) * kHalfBytes + (ks & 3) * 32) >> 4;
+          tc::mma_f16_ss(tmem + x * kTileN, tc::desc64(qb + off, q_hi), tc::desc64(kb + off, k_hi),
+                         idesc_qk, ks > 0 ? 1u : 0u);
         }
-        tc::mma_commit(&bar_s[x]);
-        ++commits_s[x];
       };
-      auto mma_pv = [&](int x, int t) {
-        const uint32_t v_addr = tc::smem_u32(ring + ((2 * t + 1) % kRingSlots) * kTileBytes);
+      // k-steps [k0, k1) of O_x += P_x V, V in ring slot `slot`
+      auto pv_steps = [&](int x, int slot, int k0, int k1, uint32_t accumulate) {
+        const uint32_t vb = v_lo + slot * kTileStep;
 #pragma unroll
-        for (int ks = 0; ks < kTileN / 16; ++ks) {
-          const uint64_t bdesc = tc::smem_desc_sw128(v_addr + ks * 2048, kHalfBytes, 1024);
-          const uint32_t acc = (t > 0 || ks > 0) ? 1u : 0u;
+        for (int ks = k0; ks < k1; ++ks) {
+          const uint64_t bdesc = tc::desc64(vb + ks * (2048 >> 4), v_hi);
+          const uint32_t acc = ks > 0 ? 1u : accumulate;
           if constexpr (kPTmem) {
             // P_x over the first 64 columns of S_x: 8 columns (16 keys) per step
             tc::mma_f16_ts(tmem + 2 * kTileN + x * kHeadDim, tmem + x * kTileN + ks * 8, bdesc,
                            idesc_pv, acc);
           } else {
-            const uint32_t aoff = (ks >> 2) * kHalfBytes + (ks & 3) * 32;
+            const uint32_t off = ((ks >> 2) * kHalfBytes + (ks & 3) * 32) >> 4;
             tc::mma_f16_ss(tmem + 2 * kTileN + x * kHeadDim,
-                           tc::smem_desc_sw128(tc::smem_u32(smem + (2 + x) * kTileBytes) + aoff,
-                                               16, 1024),
-                           bdesc, idesc_pv, acc);
+                           tc::desc64(q_lo + (2 + x) * kTileStep + off, q_hi), bdesc, idesc_pv, acc);
           }
         }
+      };
+      auto commit_s = [&](int x) {
+        tc::mma_commit(&bar_s[x]);
+        ++commits_s[x];
+      };
+      auto commit_pv = [&](int x) {
         tc::mma_commit(&bar_pv[x]);
         ++commits_pv[x];
+      };
+      // Once P_x(t) is ready: PV_x(t) and, unless t is the last key tile,
+      // S_x(t+1). With P in TMEM, P_x(t) occupies S_x's columns, so S_x(t+1)
+      // must follow PV_x(t). With P in shared memory, S_x(t+1) goes first
+      // (the next softmax of tile x waits on it, not on PV) and the two are
+      // interleaved four k-steps at a time: a run of eight MMAs of one
+      // B-operand major-ness followed by eight of the other costs the tensor
+      // core about 30 cycles per MMA, runs of four or less cost nothing.
+      auto after_p = [&](int x, int v_slot, int k_slot, bool more, uint32_t accumulate) {
+        if constexpr (kPTmem) {
+          pv_steps(x, v_slot, 0, 8, accumulate);
+          commit_pv(x);
+          if (more) {
+            s_steps(x, k_slot, 0, 8);
+            commit_s(x);
+          }
+        } else if (more) {
+          s_steps(x, k_slot, 0, 4);
+          pv_steps(x, v_slot, 0, 4, accumulate);
+          s_steps(x, k_slot, 4, 8);
+          commit_s(x);
+          pv_steps(x, v_slot, 4, 8, 1u);
+          commit_pv(x);
+        } else {
+          pv_steps(x, v_slot, 0, 8, accumulate);
+          commit_pv(x);
+        }
       };
       bool ok = tc::mbar_wait(&bar_q, 0, kWaitLimit) && wait_item(0);
       if (ok) {
         tc::tc_fence_after();
-        mma_s(0, 0);
-        mma_s(1, 0);
+        s_steps(0, 0, 0, 8);
+        commit_s(0);
+        s_steps(1, 0, 0, 8);
+        commit_s(1);
         tc::mma_commit(&bar_empty[0]);  // K(0) read by both S MMAs
       }
+      // ring slots of V(t) and K(t+1): items 2t+1 and 2t+2
+      int v_slot = 1 % kRingSlots;
       for (int t = 0; ok && t < n_tiles; ++t) {
-        ok = tc::mbar_wait(&bar_p[0], t & 1, kWaitLimit) && wait_item(2 * t + 1);
+        const int k_next = v_slot + 1 == kRingSlots ? 0 : v_slot + 1;
+        const bool more = t + 1 < n_tiles;
+        const uint32_t accumulate = t > 0 ? 1u : 0u;
+        ok = tc::mbar_wait(&bar_p[0], t & 1, kWaitLimit) && wait_item(2 * t + 1) &&
+             (!more || wait_item(2 * t + 2));
         if (!ok) break;
         tc::tc_fence_after();
-        mma_pv(0, t);
-        if (t + 1 < n_tiles) {
-          ok = wait_item(2 * t + 2);
-          if (!ok) break;
-          tc::tc_fence_after();
-          mma_s(0, t + 1);
-        }
+        after_p(0, v_slot, k_next, more, accumulate);
         ok = tc::mbar_wait(&bar_p[1], t & 1, kWaitLimit);
         if (!ok) break;
         tc::tc_fence_after();
-        mma_pv(1, t);
-        tc::mma_commit(&bar_empty[(2 * t + 1) % kRingSlots]);  // V(t) read by both PV MMAs
-        if (t + 1 < n_tiles) {
-          mma_s(1, t + 1);
-          tc::mma_commit(&bar_empty[(2 * t + 2) % kRingSlots]);  // K(t+1) read by both S MMAs
-        }
+        after_p(1, v_slot, k_next, more, accumulate);
+        tc::mma_commit(&bar_empty[v_slot]);  // V(t) read by both PV MMAs
+        if (more) tc::mma_commit(&bar_empty[k_next]);  // K(t+1) read by both S MMAs
+        v_slot = k_next + 1 == kRingSlots ? 0 : k_next + 1;
       }
       if (!ok) {
         *aborted = 1;
@@ -694,6 +754,7 @@ __global__ void __launch_bounds__(kPairThreads, 1)
       // keys past the causal limit somewhere in the warp (warp-uniform, so the
       // TMEM collectives below never sit under a divergent branch)
       const bool diagonal = __any_sync(kFullMask, n0 + kTileN - 1 > row_limit);
+      // row max, 64 columns per TMEM wait
       float mx = -INFINITY;
 #pragma unroll
       for (int hb = 0; hb < 2; ++hb) {
@@ -749,7 +810,7 @@ __global__ void __launch_bounds__(kPairThreads, 1)
       const uint64_t scale2 = pk2(p.scale_log2, p.scale_log2);
       const uint64_t neg2 = pk2(neg_mref, neg_mref);
 #pragma unroll
-      for (int cc = 0; cc < 4; ++cc) {  // one 32-column chunk per TMEM wait: fewer live registers
+      for (int cc = 0; cc < 4; ++cc) {  // 32-column chunks
         uint32_t sr[32];
         tc::tmem_ld32(s_tmem + cc * 32, sr);
         tc::tmem_ld_wait(sr);

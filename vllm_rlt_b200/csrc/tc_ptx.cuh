@@ -218,6 +218,15 @@ __device__ __forceinline__ uint64_t smem_desc_sw128(uint32_t addr, uint32_t lbo,
   return d;
 }
 
+// A descriptor from its two words. The start address occupies the low 14
+// bits of the low word and stays below 2^14 for any shared-memory address,
+// so moving an operand is a 32-bit add on the low word.
+__device__ __forceinline__ uint64_t desc64(uint32_t lo, uint32_t hi) {
+  uint64_t d;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(d) : "r"(lo), "r"(hi));
+  return d;
+}
+
 // kind::f16 instruction descriptor: fp32 accumulator, A/B of format `fmt`
 // (0 = f16, 1 = bf16), A K-major, B K-major (b_mn = 0) or MN-major (b_mn = 1).
 __host__ __device__ constexpr uint32_t idesc_f16(uint32_t fmt, uint32_t m, uint32_t n,
