@@ -509,7 +509,7 @@ __global__ void __launch_bounds__(kPairThreads, 1)
     }
     for (int x = 0; x < 2; ++x) {
       tc::mbar_init(&bar_s[x], 1);
-      tc::mbar_init(&bar_p[x], kTileM);
+      tc::mbar_init(&bar_p[x], kTileM / 32);  // one arrival per softmax warp
       tc::mbar_init(&bar_pv[x], 1);
     }
     tc::fence_mbar_init();
@@ -558,6 +558,11 @@ __global__ void __launch_bounds__(kPairThreads, 1)
       }
       return blk;
     };
+    if (lane == 0) {
+      tc::prefetch_tensormap(&p.qmap);
+      tc::prefetch_tensormap(&p.kmap);
+      tc::prefetch_tensormap(&p.vmap);
+    }
     int cur = tile_pages(0);
     int nxt = tile_pages(1);
     if (lane == 0) {
@@ -856,7 +861,8 @@ __global__ void __launch_bounds__(kPairThreads, 1)
       else
         tc::fence_proxy_async_smem();
       tc::tc_fence_before();
-      tc::mbar_arrive(&bar_p[x]);
+      __syncwarp();  // every lane's P is written before the warp's single arrival
+      if (lane == 0) tc::mbar_arrive(&bar_p[x]);
     }
     if (t == n_tiles) {
       if (!__all_sync(kFullMask, tc::mbar_wait(&bar_pv[x], (n_tiles - 1) & 1, kWaitLimit)))
