@@ -101,36 +101,6 @@ __device__ __forceinline__ float max3(float a, float b, float c) {
   return r;
 }
 
-// 2^x for two lanes without the XU unit (which executes MUFU ex2 and also
-// every float<->int conversion and rounding instruction): x is clamped to
-// [-126, +inf), rounded to the nearest integer i by adding 1.5 * 2^23 (the
-// sum's low mantissa bits then hold i), f = x - i lies in [-1/2, 1/2], and
-// 2^f ~= 1 + f (c1 + f (c2 + f c3)) -- a cubic fitted here to the relative
-// error of 2^f on [-1/2, 1/2] by iteratively reweighted least squares
-// (Lawson), max relative error 1.0e-4, far below the bf16/fp16 rounding of
-// P. 2^i is added to the exponent field with integer arithmetic.
-__device__ __forceinline__ uint64_t exp2_poly2(uint64_t x2) {
-  constexpr float c1 = 0.693282902f, c2 = 0.242210627f, c3 = 0.0550086908f;
-  constexpr float kMagic = 12582912.0f;  // 1.5 * 2^23
-  float x0, x1;
-  upk2(x2, x0, x1);
-  const uint64_t x = pk2(fmaxf(x0, -126.f), fmaxf(x1, -126.f));
-  const uint64_t t = add2(x, pk2(kMagic, kMagic));  // round to nearest integer
-  const uint64_t r = add2(t, pk2(-kMagic, -kMagic));
-  const uint64_t f = fma2(r, pk2(-1.f, -1.f), x);   // x - round(x)
-  uint64_t q = fma2(pk2(c3, c3), f, pk2(c2, c2));
-  q = fma2(q, f, pk2(c1, c1));
-  q = fma2(q, f, pk2(1.f, 1.f));
-  float q0, q1, t0, t1;
-  upk2(q, q0, q1);
-  upk2(t, t0, t1);
-  // exponent += i, with i = bits(t) - bits(kMagic)
-  const uint32_t bias = __float_as_uint(kMagic) << 23;
-  q0 = __uint_as_float(__float_as_uint(q0) + (__float_as_uint(t0) << 23) - bias);
-  q1 = __uint_as_float(__float_as_uint(q1) + (__float_as_uint(t1) << 23) - bias);
-  return pk2(q0, q1);
-}
-
 template <typename T>
 struct Fmt;
 template <>
@@ -808,9 +778,12 @@ __global__ void __launch_bounds__(kPairThreads, 1)
           tc::tmem_st_wait();
         }
       }
-      // probabilities p = 2^(s * scale_log2 - m) -> P_x (swizzled), row sum.
-      // Half of the column pairs take ex2 on the MUFU unit, the other half
-      // the FMA-pipe polynomial; arguments and sums use packed fp32x2 ops.
+      // probabilities p = 2^(s * scale_log2 - m) -> P_x, row sum. Every
+      // exponential runs on the MUFU unit: a polynomial on the FMA pipe needs
+      // integer and min/max work on the ALU pipe, which the row max and the
+      // P conversion already keep busy, and measured slower at every split
+      // tried (1/8 to 1/2 of the columns). Arguments and sums use packed
+      // fp32x2 ops.
       uint64_t psum2 = pk2(0.f, 0.f);
       const uint64_t scale2 = pk2(p.scale_log2, p.scale_log2);
       const uint64_t neg2 = pk2(neg_mref, neg_mref);
@@ -825,14 +798,9 @@ __global__ void __launch_bounds__(kPairThreads, 1)
           const uint64_t arg =
               fma2(pk2(__uint_as_float(sr[j]), __uint_as_float(sr[j + 1])), scale2, neg2);
           float p0, p1;
-          if ((j & 2) == 0) {
-            float a0, a1;
-            upk2(arg, a0, a1);
-            p0 = ex2(a0);
-            p1 = ex2(a1);
-          } else {
-            upk2(exp2_poly2(arg), p0, p1);
-          }
+          upk2(arg, p0, p1);
+          p0 = ex2(p0);
+          p1 = ex2(p1);
           if (diagonal) {
             const int key = n0 + cc * 32 + j;
             p0 = key <= row_limit ? p0 : 0.f;
