@@ -23,6 +23,7 @@
 
 #include <atomic>
 #include <mutex>
+#include <type_traits>
 
 #include "common.cuh"
 #include "tc_ptx.cuh"
@@ -729,28 +730,40 @@ __global__ void __launch_bounds__(kPairThreads, 1)
       // keys past the causal limit somewhere in the warp (warp-uniform, so the
       // TMEM collectives below never sit under a divergent branch)
       const bool diagonal = __any_sync(kFullMask, n0 + kTileN - 1 > row_limit);
-      // row max, 64 columns per TMEM wait
-      float mx = -INFINITY;
+      // Row max, 64 columns per TMEM wait. The pass exists in two
+      // instantiations, with and without the causal mask, chosen by one
+      // warp-uniform branch: a mask test inside the unrolled loops was
+      // predicated into every key tile, not just the diagonal ones.
+      auto row_max = [&](auto masked) {
+        constexpr bool kMasked = decltype(masked)::value;
+        float m = -INFINITY;
 #pragma unroll
-      for (int hb = 0; hb < 2; ++hb) {
-        uint32_t sr[2][32];
-        tc::tmem_ld32(s_tmem + hb * 64, sr[0]);
-        tc::tmem_ld32(s_tmem + hb * 64 + 32, sr[1]);
-        tc::tmem_ld_wait(sr[0]);
-        tc::tmem_ld_wait(sr[1]);
-        if (diagonal) {
+        for (int hb = 0; hb < 2; ++hb) {
+          uint32_t sr[2][32];
+          tc::tmem_ld32(s_tmem + hb * 64, sr[0]);
+          tc::tmem_ld32(s_tmem + hb * 64 + 32, sr[1]);
+          tc::tmem_ld_wait(sr[0]);
+          tc::tmem_ld_wait(sr[1]);
+          if constexpr (kMasked) {
+#pragma unroll
+            for (int c = 0; c < 2; ++c)
+#pragma unroll
+              for (int j = 0; j < 32; ++j)
+                if (n0 + hb * 64 + c * 32 + j > row_limit) sr[c][j] = __float_as_uint(-INFINITY);
+          }
 #pragma unroll
           for (int c = 0; c < 2; ++c)
 #pragma unroll
-            for (int j = 0; j < 32; ++j)
-              if (n0 + hb * 64 + c * 32 + j > row_limit) sr[c][j] = __float_as_uint(-INFINITY);
+            for (int j = 0; j < 32; j += 2)
+              m = max3(m, __uint_as_float(sr[c][j]), __uint_as_float(sr[c][j + 1]));
         }
-#pragma unroll
-        for (int c = 0; c < 2; ++c)
-#pragma unroll
-          for (int j = 0; j < 32; j += 2)
-            mx = max3(mx, __uint_as_float(sr[c][j]), __uint_as_float(sr[c][j + 1]));
-      }
+        return m;
+      };
+      float mx;
+      if (diagonal)
+        mx = row_max(std::true_type{});
+      else
+        mx = row_max(std::false_type{});
       const float m_new = fmaxf(m_used, mx * p.scale_log2);
       float factor = 1.f;
       if (m_new > m_used + 8.f) {
@@ -784,45 +797,53 @@ __global__ void __launch_bounds__(kPairThreads, 1)
       // P conversion already keep busy, and measured slower at every split
       // tried (1/8 to 1/2 of the columns). Arguments and sums use packed
       // fp32x2 ops.
-      uint64_t psum2 = pk2(0.f, 0.f);
       const uint64_t scale2 = pk2(p.scale_log2, p.scale_log2);
       const uint64_t neg2 = pk2(neg_mref, neg_mref);
+      auto probabilities = [&](auto masked) {
+        constexpr bool kMasked = decltype(masked)::value;
+        uint64_t psum2 = pk2(0.f, 0.f);
 #pragma unroll
-      for (int cc = 0; cc < 4; ++cc) {  // 32-column chunks
-        uint32_t sr[32];
-        tc::tmem_ld32(s_tmem + cc * 32, sr);
-        tc::tmem_ld_wait(sr);
-        uint32_t packed[16];
+        for (int cc = 0; cc < 4; ++cc) {  // 32-column chunks
+          uint32_t sr[32];
+          tc::tmem_ld32(s_tmem + cc * 32, sr);
+          tc::tmem_ld_wait(sr);
+          uint32_t packed[16];
 #pragma unroll
-        for (int j = 0; j < 32; j += 2) {
-          const uint64_t arg =
-              fma2(pk2(__uint_as_float(sr[j]), __uint_as_float(sr[j + 1])), scale2, neg2);
-          float p0, p1;
-          upk2(arg, p0, p1);
-          p0 = ex2(p0);
-          p1 = ex2(p1);
-          if (diagonal) {
-            const int key = n0 + cc * 32 + j;
-            p0 = key <= row_limit ? p0 : 0.f;
-            p1 = key + 1 <= row_limit ? p1 : 0.f;
+          for (int j = 0; j < 32; j += 2) {
+            const uint64_t arg =
+                fma2(pk2(__uint_as_float(sr[j]), __uint_as_float(sr[j + 1])), scale2, neg2);
+            float p0, p1;
+            upk2(arg, p0, p1);
+            p0 = ex2(p0);
+            p1 = ex2(p1);
+            if constexpr (kMasked) {
+              const int key = n0 + cc * 32 + j;
+              p0 = key <= row_limit ? p0 : 0.f;
+              p1 = key + 1 <= row_limit ? p1 : 0.f;
+            }
+            psum2 = add2(psum2, pk2(p0, p1));
+            packed[j / 2] = pack2<T>(p0, p1);
           }
-          psum2 = add2(psum2, pk2(p0, p1));
-          packed[j / 2] = pack2<T>(p0, p1);
-        }
-        if constexpr (kPTmem) {
-          // P columns [16 cc, 16 cc + 16) of S_x: S columns this thread already read
-          tc::tmem_st16(s_tmem + cc * 16, packed);
-        } else {
-          uint8_t* base = smem + (2 + x) * kTileBytes + (cc >> 1) * kHalfBytes;  // P_x
+          if constexpr (kPTmem) {
+            // P columns [16 cc, 16 cc + 16) of S_x: S columns this thread already read
+            tc::tmem_st16(s_tmem + cc * 16, packed);
+          } else {
+            uint8_t* base = smem + (2 + x) * kTileBytes + (cc >> 1) * kHalfBytes;  // P_x
 #pragma unroll
-          for (int v = 0; v < 4; ++v)
-            *reinterpret_cast<uint4*>(base + sw128(r, (cc & 1) * 4 + v)) =
-                make_uint4(packed[4 * v], packed[4 * v + 1], packed[4 * v + 2], packed[4 * v + 3]);
+            for (int v = 0; v < 4; ++v)
+              *reinterpret_cast<uint4*>(base + sw128(r, (cc & 1) * 4 + v)) =
+                  make_uint4(packed[4 * v], packed[4 * v + 1], packed[4 * v + 2], packed[4 * v + 3]);
+          }
         }
-      }
-      float psum_lo, psum_hi;
-      upk2(psum2, psum_lo, psum_hi);
-      const float psum = psum_lo + psum_hi;
+        float lo, hi;
+        upk2(psum2, lo, hi);
+        return lo + hi;
+      };
+      float psum;
+      if (diagonal)
+        psum = probabilities(std::true_type{});
+      else
+        psum = probabilities(std::false_type{});
       l_sum = l_sum * factor + psum;
       if constexpr (kPTmem)
         tc::tmem_st_wait();
