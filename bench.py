@@ -53,10 +53,10 @@ def parse():
     p.add_argument("--rows", type=int, default=256)
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--no-extras", action="store_true",
-                   help="skip the prefill and long-context sub-measurements")
-    p.add_argument("--workload", choices=["decode", "prefill", "longctx", "ouro"],
+                   help="skip the Ouro, prefill, long-context and shared-prefix sub-measurements")
+    p.add_argument("--workload", choices=["decode", "prefill", "longctx", "ouro", "shared"],
                    default="decode",
-                   help="decode: the headline line; prefill/longctx: that workload alone")
+                   help="decode: the headline line; the others: that workload alone")
     return p.parse_args()
 
 
@@ -360,6 +360,81 @@ def longctx_extra(device, steps, warmup, rank, world):
     }
 
 
+def shared_extra(device, steps, warmup, rank):
+    """Prefix-cached decode (configs[1] geometry): 256 rows in 16 groups of 16
+    that share a system prompt of U[1024, 4096] tokens (the same physical
+    pages, as prefix caching hands out), each row then its own
+    lognormal(median 512, sigma 0.6) suffix in [16, 4096]. Times the
+    shared-prefix path against the plain decode kernel on the same inputs."""
+    import torch
+
+    import vllm_rlt_b200 as rb
+    from vllm_rlt_b200.kernels.paged_attention import decode_bytes
+
+    page, hkv, d = 16, 16, 128
+    rng = np.random.default_rng(21)
+    groups, per_group = 16, 16
+    prompt = (rng.integers(1024, 4097, size=groups) // page) * page
+    suffix = np.clip(np.exp(rng.normal(np.log(512), 0.6, size=groups * per_group)), 16, 4096)
+    suffix = suffix.astype(np.int64)
+    lengths = np.repeat(prompt, per_group) + suffix
+    shared_pages = prompt // page
+    own_pages = [int(math.ceil(int(n) / page)) for n in suffix]
+    num_blocks = int(shared_pages.sum() + sum(own_pages) + groups * per_group)
+    width = int(max(int(math.ceil(int(n) / page)) for n in lengths))
+    perm = rng.permutation(num_blocks)
+    tables = np.full((groups * per_group, width), -1, dtype=np.int32)
+    c = 0
+    group_pages = []
+    for gi in range(groups):
+        group_pages.append(perm[c : c + shared_pages[gi]])
+        c += shared_pages[gi]
+    for r in range(groups * per_group):
+        gi = r // per_group
+        n_total = int(math.ceil(int(lengths[r]) / page))
+        tables[r, : shared_pages[gi]] = group_pages[gi]
+        extra = n_total - shared_pages[gi]
+        tables[r, shared_pages[gi] : n_total] = perm[c : c + extra]
+        c += extra
+    g = torch.Generator(device=device).manual_seed(31 + rank)
+    key = torch.empty((num_blocks, 1, page, hkv, d), device=device, dtype=torch.bfloat16)
+    value = torch.empty_like(key)
+    fill_random(key, g)
+    fill_random(value, g)
+    q = torch.empty((len(lengths), hkv, d), device=device, dtype=torch.bfloat16)
+    fill_random(q, g)
+    t_tables = torch.from_numpy(tables).to(device)
+    t_lengths = torch.from_numpy(lengths.astype(np.int32)).to(device)
+    import time as _time
+    t0 = _time.perf_counter()
+    plan = rb.plan_shared_prefix(tables, lengths, page, hkv, hkv, device)
+    plan_ms = (_time.perf_counter() - t0) * 1e3
+    backend = rb.B200PagedAttention(device, torch.bfloat16, d, page)
+    ms_shared = time_region(
+        lambda: rb.paged_attention_shared(q, key[:, 0], value[:, 0], t_tables, plan), steps,
+        warmup, device)
+    ms_plain = time_region(lambda: backend(q, key[:, 0], value[:, 0], t_tables, t_lengths), steps,
+                           warmup, device)
+    logical = decode_bytes(lengths, page, hkv, d, 2)
+    read = plan.read_tokens * hkv * d * 2 * 2
+    peak, kind = measured_peak()
+    return {
+        "workload": "configs[1] geometry with prefix caching: 256 rows = 16 groups x 16 sharing a "
+                    "U[1024,4096]-token prompt, own suffix lognormal(512, 0.6) in [16, 4096]",
+        "rows": int(len(lengths)), "sum_ctx": int(lengths.sum()),
+        "kv_rows_read_over_logical": round(plan.read_tokens / plan.logical_tokens, 4),
+        "ms_per_step": round(ms_shared, 4), "ms_per_step_plain_decode": round(ms_plain, 4),
+        "speedup_vs_plain_decode": round(ms_plain / ms_shared, 3),
+        "value": round(logical / (ms_shared / 1e3) / 1e9, 1),
+        "unit": "GB/s (logical: every row's K/V counted, as a per-row decode reads it)",
+        "hbm": {"achieved": round(read / (ms_shared / 1e3) / 1e9, 1), "peak": peak,
+                "unit": "GB/s", "frac": round(read / (ms_shared / 1e3) / 1e9 / peak, 4),
+                "peak_kind": kind, "bytes": "K/V token rows the plan reads, once per group"},
+        "plan_ms_host": round(plan_ms, 2),
+        "errors": backend.check_errors(),
+    }
+
+
 def ouro_extra(device, steps, warmup, rank, requests=64):
     """random-init Ouro-1.4B-shaped mixed-depth decode. 64 resident
     requests per GPU (LAST-EXITED needs ~1.6 GB of KV per request at 4 planes
@@ -454,6 +529,8 @@ def run_ours(args):
             res = prefill_extra(device, args.steps, args.warmup, rank)
         elif args.workload == "ouro":
             res = ouro_extra(device, args.steps, args.warmup, rank)
+        elif args.workload == "shared":
+            res = shared_extra(device, args.steps, args.warmup, rank)
         else:
             res = longctx_extra(device, args.steps, args.warmup, rank, world)
         if world > 1:
@@ -582,7 +659,8 @@ def run_ours(args):
         torch.cuda.empty_cache()
         for name, fn in (("ouro", lambda: ouro_extra(device, 30, 3, rank)),
                          ("prefill", lambda: prefill_extra(device, 10, 3, rank)),
-                         ("longctx", lambda: longctx_extra(device, 20, 5, rank, world))):
+                         ("longctx", lambda: longctx_extra(device, 20, 5, rank, world)),
+                         ("shared_prefix", lambda: shared_extra(device, 20, 5, rank))):
             try:
                 extras[name] = fn()
             except Exception as error:  # reported, never silently dropped

@@ -90,6 +90,23 @@ int rlt_paged_decode(const void* q, const void* key_cache, const void* value_cac
                      int64_t table_row_stride, int64_t out_row_stride, int64_t out_head_stride,
                      float scale, void* stream);
 
+/* rlt_paged_decode that also writes, per row and query head, the base-2
+ * log-sum-exp of the scaled scores, lse[row * Hq + h] = max + log2(sum) in
+ * units of scale * log2(e) (-inf for an empty row), so that attention over
+ * disjoint token ranges can be merged exactly. lse must not be NULL. The
+ * reference's torch path computes the same quantity inside its softmax
+ * (vllm_rlt/kernels/paged_attention.py:12-36) without returning it. */
+int rlt_paged_decode_lse(const void* q, const void* key_cache, const void* value_cache,
+                         const int32_t* block_tables, const int32_t* context_lengths, void* out,
+                         void* workspace, size_t workspace_bytes, int32_t* status, int32_t dtype,
+                         int32_t num_rows, int32_t num_q_heads, int32_t num_kv_heads,
+                         int32_t head_dim, int32_t page_size, int32_t table_width,
+                         int64_t num_blocks, int64_t q_row_stride, int64_t q_head_stride,
+                         int64_t k_block_stride, int64_t k_token_stride, int64_t k_head_stride,
+                         int64_t v_block_stride, int64_t v_token_stride, int64_t v_head_stride,
+                         int64_t table_row_stride, int64_t out_row_stride,
+                         int64_t out_head_stride, float scale, float* lse, void* stream);
+
 /* Bytes of scratch rlt_paged_prefill needs: per-token (table row, causal
  * length) pairs plus the split-KV partials of the CUDA-core path. */
 size_t rlt_paged_prefill_workspace_bytes(int32_t num_tokens, int32_t num_q_heads,
@@ -124,11 +141,52 @@ int rlt_paged_prefill(const void* q, const void* key_cache, const void* value_ca
  * wheel makes the same choice internally. */
 int rlt_paged_prefill_uses_tensor_cores(int32_t dtype, int32_t head_dim, int32_t page_size);
 
-/* Diagnostics: choose the tensor-core prefill kernel for the process (2 =
- * warp-specialised two-tile kernel, the default; 1 = single-tile kernel);
- * returns the previous choice (any other value only queries). No counterpart
- * in the reference. */
+/* Diagnostics: choose the tensor-core prefill kernel for the process (3 =
+ * warp-specialised two-tile kernel with P in TMEM, the default; 2 = the same
+ * with P in shared memory; 1 = single-tile kernel); returns the previous
+ * choice (any other value only queries). No counterpart in the reference. */
 int rlt_prefill_tc_select(int32_t version);
+
+/* Decode attention that reads K/V pages shared by several rows once
+ * (prefix caching: vllm_rlt/core/kv_cache_manager.py:211-251 hands the
+ * same physical prompt pages to many requests). Same result as
+ * rlt_paged_decode (softmax(q K^T * scale) V over each row's context,
+ * vllm_rlt/kernels/paged_attention.py:12-36) for the rows the plan covers;
+ * the plan is built on the host (vllm_rlt_b200.plan_shared_prefix):
+ *   chunks[c*5 + 0..4] = table row, token begin, token end, member begin,
+ *     member count; the chunk's tokens are read once through that table row
+ *     and attended by every member row; member count * (Hq / Hkv) <= 32;
+ *   members[member begin + i] = row id (num_members entries in all);
+ *     member_slots[...] = the partial slot of that (row, chunk);
+ *     row_slots[r] .. row_slots[r + 1] = row r's slots.
+ * All plan arrays are device int32. The chunks cover only the shared
+ * prefixes: on entry `out` must hold each row's attention over its own tokens
+ * after the prefix and `suffix_lse` [rows, Hq] its base-2 log-sum-exp, as
+ * rlt_paged_decode_lse leaves them when run on the per-row suffix tables
+ * (each row's table shifted past its shared pages); the prefix partials are
+ * merged into `out` in place. Workspace: fp32 partials, size
+ * rlt_paged_decode_shared_workspace_bytes(num_slots, Hq, D). head_dim 64 or
+ * 128; K/V pointers and strides 16-byte aligned. Two kernel launches (chunk
+ * partials, merge); asynchronous, no allocation. The reference has no
+ * counterpart: its decode reads shared pages once per row. */
+size_t rlt_paged_decode_shared_workspace_bytes(int32_t num_slots, int32_t num_q_heads,
+                                               int32_t head_dim);
+int rlt_paged_decode_shared(const void* q, const void* key_cache, const void* value_cache,
+                            const int32_t* block_tables, const int32_t* chunks,
+                            const int32_t* members, const int32_t* member_slots,
+                            const int32_t* row_slots, const float* suffix_lse, void* out,
+                            void* workspace, size_t workspace_bytes, int32_t* status,
+                            int32_t dtype,
+                            int32_t num_rows, int32_t num_q_heads, int32_t num_kv_heads,
+                            int32_t head_dim, int32_t page_size, int32_t table_width,
+                            int64_t num_blocks, int32_t num_chunks, int32_t num_slots,
+                            int32_t num_members, int64_t q_row_stride, int64_t q_head_stride,
+                            int64_t k_block_stride,
+                            int64_t k_token_stride, int64_t k_head_stride,
+                            int64_t v_block_stride, int64_t v_token_stride,
+                            int64_t v_head_stride, int64_t table_row_stride,
+                            int64_t out_row_stride, int64_t out_head_stride, float scale,
+                            void* stream);
 
 /* Size of the static split-KV scratch of rlt_paged_decode_noalloc (bytes). */
 #define RLT_NOALLOC_SCRATCH_BYTES (16u << 20)

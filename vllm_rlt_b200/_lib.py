@@ -59,6 +59,13 @@ SIGNATURES = {
         + [_i64] * 12
         + [_f32, _p],
     ),
+    "rlt_paged_decode_lse": (
+        _i32,
+        [_p, _p, _p, _p, _p, _p, _p, _sz, _p, _i32]
+        + [_i32] * 6
+        + [_i64] * 12
+        + [_f32, _p, _p],
+    ),
     "rlt_paged_decode_noalloc": (_i32, [_p] * 7 + [_i32] * 7 + [_i64] * 12 + [_f32, _p]),
     "rlt_paged_prefill_workspace_bytes": (_sz, [_i32, _i32, _i32, _i32, _i32]),
     "rlt_paged_prefill": (
@@ -67,6 +74,11 @@ SIGNATURES = {
     ),
     "rlt_paged_prefill_uses_tensor_cores": (_i32, [_i32, _i32, _i32]),
     "rlt_prefill_tc_select": (_i32, [_i32]),
+    "rlt_paged_decode_shared_workspace_bytes": (_sz, [_i32, _i32, _i32]),
+    "rlt_paged_decode_shared": (
+        _i32,
+        [_p] * 11 + [_sz, _p] + [_i32] * 7 + [_i64] + [_i32] * 3 + [_i64] * 11 + [_f32, _p],
+    ),
     "rlt_kv_write": (_i32, [_p] * 7 + [_i32] * 6 + [_i64] * 9 + [_p]),
     "rlt_finalize": (_i32, [_p] * 5 + [_i32] * 8 + [_i64] * 4 + [_p]),
     "rlt_metadata": (_i32, [_p] * 9 + [_i32] * 7 + [_p]),

@@ -59,6 +59,8 @@ struct DecodeParams {
   float* ws_o;   // [rows, launch_splits, hq, head_dim] unnormalised acc
   float* ws_ml;  // [rows, launch_splits, hq, 2] (running max in log2 units, sum)
   int* counters;  // [rows, hq] finished-split counts (zeroed by the launcher)
+  float* lse;     // optional [rows, hq]: base-2 log-sum-exp of the scaled scores
+                  // (max + log2(sum)); -inf for an empty row. NULL: not written
   int32_t* status;
   int rows, hq, hkv, group, head_dim, page, width, launch_splits;
   int64_t num_blocks;
@@ -138,6 +140,8 @@ __device__ __forceinline__ void merge_splits(const DecodeParams& p, int row, int
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) total += __shfl_xor_sync(kFullMask, total, o);
   const float inv = 1.f / fmaxf(total, 1e-30f);
+  if (p.lse != nullptr && lane == 0)
+    p.lse[static_cast<int64_t>(row) * p.hq + qh] = mx == -INFINITY ? -INFINITY : mref + __log2f(total);
   T* out = static_cast<T*>(p.out) + row * p.o_rs + qh * p.o_hs;
   for (int d4 = lane; d4 < p.head_dim / 4; d4 += 32) {
     float4 a = make_float4(0.f, 0.f, 0.f, 0.f);
@@ -197,6 +201,10 @@ __global__ void __launch_bounds__(kDecodeWarps * 32, RLT_DECODE_MIN_BLOCKS)
 #pragma unroll
       for (int c = 0; c < GC; ++c)
         st_vec(out + row * p.o_rs + (qh0 + c) * p.o_hs + s * VEC, pack16<T>(zero));
+    }
+    if (p.lse != nullptr && active && split == 0 && lane == 0) {
+#pragma unroll
+      for (int c = 0; c < GC; ++c) p.lse[static_cast<int64_t>(row) * p.hq + qh0 + c] = -INFINITY;
     }
     return;
   }
@@ -418,6 +426,11 @@ __global__ void __launch_bounds__(kDecodeWarps * 32, RLT_DECODE_MIN_BLOCKS)
         st_vec(out + row * p.o_rs + (qh0 + c) * p.o_hs + s * VEC, pack16<T>(o));
       }
     }
+    if (p.lse != nullptr && active && lane == 0) {
+#pragma unroll
+      for (int c = 0; c < GC; ++c)
+        p.lse[static_cast<int64_t>(row) * p.hq + qh0 + c] = m[c] + __log2f(lsum[c]);
+    }
     return;
   }
   const int64_t slot = (static_cast<int64_t>(row) * p.launch_splits + split) * p.hq + qh0;
@@ -505,6 +518,8 @@ __global__ void __launch_bounds__(128) paged_decode_generic_kernel(const __grid_
   }
   T* op = static_cast<T*>(p.out) + row * p.o_rs + qh * p.o_hs;
   const float inv = 1.f / fmaxf(l, 1e-30f);
+  if (p.lse != nullptr && lane == 0)
+    p.lse[static_cast<int64_t>(row) * p.hq + qh] = l > 0.f ? m + __log2f(l) : -INFINITY;
 #pragma unroll
   for (int i = 0; i < 8; ++i) {
     const int d = lane + 32 * i;
@@ -754,6 +769,38 @@ extern "C" size_t rlt_paged_decode_workspace_bytes(int32_t num_rows, int32_t num
   return split_bytes(num_rows, num_q_heads, head_dim, page_size, table_width);
 }
 
+namespace {
+int paged_decode_entry(const void* q, const void* key_cache, const void* value_cache,
+                       const int32_t* block_tables, const int32_t* context_lengths, void* out,
+                       void* workspace, size_t workspace_bytes, int32_t* status, int32_t dtype,
+                       int32_t num_rows, int32_t num_q_heads, int32_t num_kv_heads,
+                       int32_t head_dim, int32_t page_size, int32_t table_width,
+                       int64_t num_blocks, int64_t q_row_stride, int64_t q_head_stride,
+                       int64_t k_block_stride, int64_t k_token_stride, int64_t k_head_stride,
+                       int64_t v_block_stride, int64_t v_token_stride, int64_t v_head_stride,
+                       int64_t table_row_stride, int64_t out_row_stride,
+                       int64_t out_head_stride, float scale, float* lse, void* stream) {
+  const DecodeArgs a{q, key_cache, value_cache, block_tables, status, dtype, num_rows,
+                     num_q_heads, num_kv_heads, head_dim, page_size, table_width, num_blocks,
+                     q_row_stride, q_head_stride, k_block_stride, k_token_stride, k_head_stride,
+                     v_block_stride, v_token_stride, v_head_stride, table_row_stride,
+                     out_row_stride, out_head_stride, out, scale};
+  const int bad = validate(a);
+  if (bad != RLT_OK) return bad;
+  if (num_rows == 0) return RLT_OK;
+  bool fast = false;
+  DecodeParams p = make_params(a, &fast);
+  p.lengths = context_lengths;
+  p.lse = lse;
+  if (p.launch_splits > 1) {
+    const size_t need = split_bytes(num_rows, num_q_heads, head_dim, page_size, table_width);
+    if (workspace == nullptr || workspace_bytes < need || !aligned16(workspace))
+      return RLT_E_WORKSPACE;
+  }
+  return run(p, dtype, fast, workspace, static_cast<cudaStream_t>(stream));
+}
+}  // namespace
+
 extern "C" int rlt_paged_decode(const void* q, const void* key_cache, const void* value_cache,
                                 const int32_t* block_tables, const int32_t* context_lengths,
                                 void* out, void* workspace, size_t workspace_bytes,
@@ -766,23 +813,36 @@ extern "C" int rlt_paged_decode(const void* q, const void* key_cache, const void
                                 int64_t v_token_stride, int64_t v_head_stride,
                                 int64_t table_row_stride, int64_t out_row_stride,
                                 int64_t out_head_stride, float scale, void* stream) {
-  const DecodeArgs a{q, key_cache, value_cache, block_tables, status, dtype, num_rows,
-                     num_q_heads, num_kv_heads, head_dim, page_size, table_width, num_blocks,
-                     q_row_stride, q_head_stride, k_block_stride, k_token_stride, k_head_stride,
-                     v_block_stride, v_token_stride, v_head_stride, table_row_stride,
-                     out_row_stride, out_head_stride, out, scale};
-  const int bad = validate(a);
-  if (bad != RLT_OK) return bad;
-  if (num_rows == 0) return RLT_OK;
-  bool fast = false;
-  DecodeParams p = make_params(a, &fast);
-  p.lengths = context_lengths;
-  if (p.launch_splits > 1) {
-    const size_t need = split_bytes(num_rows, num_q_heads, head_dim, page_size, table_width);
-    if (workspace == nullptr || workspace_bytes < need || !aligned16(workspace))
-      return RLT_E_WORKSPACE;
-  }
-  return run(p, dtype, fast, workspace, static_cast<cudaStream_t>(stream));
+  return paged_decode_entry(q, key_cache, value_cache, block_tables, context_lengths, out,
+                            workspace, workspace_bytes, status, dtype, num_rows, num_q_heads,
+                            num_kv_heads, head_dim, page_size, table_width, num_blocks,
+                            q_row_stride, q_head_stride, k_block_stride, k_token_stride,
+                            k_head_stride, v_block_stride, v_token_stride, v_head_stride,
+                            table_row_stride, out_row_stride, out_head_stride, scale, nullptr,
+                            stream);
+}
+
+extern "C" int rlt_paged_decode_lse(const void* q, const void* key_cache, const void* value_cache,
+                                    const int32_t* block_tables, const int32_t* context_lengths,
+                                    void* out, void* workspace, size_t workspace_bytes,
+                                    int32_t* status, int32_t dtype, int32_t num_rows,
+                                    int32_t num_q_heads, int32_t num_kv_heads, int32_t head_dim,
+                                    int32_t page_size, int32_t table_width, int64_t num_blocks,
+                                    int64_t q_row_stride, int64_t q_head_stride,
+                                    int64_t k_block_stride, int64_t k_token_stride,
+                                    int64_t k_head_stride, int64_t v_block_stride,
+                                    int64_t v_token_stride, int64_t v_head_stride,
+                                    int64_t table_row_stride, int64_t out_row_stride,
+                                    int64_t out_head_stride, float scale, float* lse,
+                                    void* stream) {
+  if (lse == nullptr) return RLT_E_SHAPE;
+  return paged_decode_entry(q, key_cache, value_cache, block_tables, context_lengths, out,
+                            workspace, workspace_bytes, status, dtype, num_rows, num_q_heads,
+                            num_kv_heads, head_dim, page_size, table_width, num_blocks,
+                            q_row_stride, q_head_stride, k_block_stride, k_token_stride,
+                            k_head_stride, v_block_stride, v_token_stride, v_head_stride,
+                            table_row_stride, out_row_stride, out_head_stride, scale, lse,
+                            stream);
 }
 
 extern "C" size_t rlt_paged_prefill_workspace_bytes(int32_t num_tokens, int32_t num_q_heads,

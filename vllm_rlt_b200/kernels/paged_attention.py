@@ -93,6 +93,41 @@ def paged_attention(q, key_cache, value_cache, block_tables, context_lengths, *,
     return output
 
 
+def paged_attention_lse(q, key_cache, value_cache, block_tables, context_lengths, *, out=None):
+    """``paged_attention`` that also returns, per row and query head, the
+    base-2 log-sum-exp of the scaled scores (fp32 ``[N, Hq]``; -inf for an
+    empty row): what merging attention over disjoint token ranges needs."""
+    _validate(q, key_cache, value_cache, block_tables, context_lengths)
+    if q.stride(-1) != 1:
+        q = q.contiguous()
+    output = torch.empty_like(q) if out is None else out
+    rows, hq, d = q.shape
+    lse = torch.empty((rows, hq), dtype=torch.float32, device=q.device)
+    if rows == 0:
+        return output, lse
+    tables = _as_int32(block_tables)
+    lengths = _as_int32(context_lengths)
+    lib = _lib.load()
+    device = q.device
+    page, hkv = key_cache.shape[1], key_cache.shape[2]
+    width = tables.shape[1]
+    need = lib.rlt_paged_decode_workspace_bytes(rows, hq, d, page, width)
+    workspace = torch.empty(need, dtype=torch.uint8, device=device) if need else None
+    code = lib.rlt_paged_decode_lse(
+        q.data_ptr(), key_cache.data_ptr(), value_cache.data_ptr(), tables.data_ptr(),
+        lengths.data_ptr(), output.data_ptr(), _lib.ptr(workspace), need,
+        _lib.status_word(device).data_ptr(), _lib.DTYPE_CODES[q.dtype],
+        rows, hq, hkv, d, page, width, key_cache.shape[0],
+        q.stride(0), q.stride(1),
+        key_cache.stride(0), key_cache.stride(1), key_cache.stride(2),
+        value_cache.stride(0), value_cache.stride(1), value_cache.stride(2),
+        tables.stride(0), output.stride(0), output.stride(1),
+        q.shape[-1] ** -0.5, lse.data_ptr(), _lib.stream_of(device),
+    )
+    _lib.check(code, "paged decode attention (log-sum-exp)")
+    return output, lse
+
+
 def b200_paged_attention(q, key_cache, value_cache, block_tables, context_lengths):
     """Explicit dispatch with no silent fallback, mirroring the reference's
     ``triton_paged_attention`` (vllm_rlt/kernels/paged_attention.py:39-54)."""
