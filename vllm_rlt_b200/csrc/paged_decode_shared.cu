@@ -201,33 +201,102 @@ __global__ void __launch_bounds__(kWarps * 32, 4) shared_range_kernel(const Shar
   }
 }
 
-// 16-bit K/V: the warps of a CTA split the chunk's (member, head) pairs into
-// blocks of up to 8 and, when there are few pairs, split its 32-token
-// sub-tiles between them (token splits are merged through shared memory at
-// the end). Each lane holds its own token's K row in registers (loaded once
-// per sub-tile, for all of the warp's pairs) and stages its V row into the
-// warp's shared-memory slab; the probability-weighted V sum reads that slab.
+// 16-bit K/V on the tensor cores (mma.sync m16n8k16, fp32 accumulate): a
+// chunk has at most 32 (member, query head) pairs, one or two 16-row M tiles,
+// far below the 64/128 rows of a tcgen05 tile. The CTA stages 64-token K/V
+// sub-tiles in shared memory (cp.async, double buffered; rows padded to an odd
+// number of 16-byte units so ldmatrix reads are conflict-free). Warp w takes M
+// tile w % tiles and a slice of every sub-tile's tokens: S = Q K^T (Q
+// fragments stay in registers for the whole chunk, K fragments by ldmatrix),
+// base-2 online softmax on the S fragments (a row's values sit in the 4 lanes
+// of a quad), P rounded to the input type and reused in registers as the A
+// operand of O += P V (V fragments by ldmatrix.trans). The warps of one M tile
+// merge their token slices through shared memory at the end.
 template <int D>
-struct Layout16 {
-  static constexpr int kQFloats = kMaxPairs * D;          // pre-scaled q, fp32
-  static constexpr int kSlabElems = kSubTile * D;         // one warp's V sub-tile
-  static constexpr int kBytes = kQFloats * 4 + kWarps * kSlabElems * 2;
-  // Token-split merge, reusing the same memory: with 4 splits a chunk has at
-  // most 8 pairs, with 2 splits at most 16; entries [split][pair < 16] of
-  // D + 2 floats (o, max, sum).
-  static constexpr int kCombinePairs = 16;
-  static constexpr int kCombineBytes = kWarps * kCombinePairs * (D + 2) * 4;
-  static_assert(kCombineBytes <= kBytes, "token-split merge buffer exceeds shared memory");
+struct LayoutMma {
+  static constexpr int kTokens = 64;                      // tokens per staged sub-tile
+  static constexpr int kRowBytes = D * 2 + 16;            // padded 16-bit row
+  static constexpr int kTileBytes = kTokens * kRowBytes;  // one K or V sub-tile
+  static constexpr int kQBytes = kMaxPairs * kRowBytes;
+  static constexpr int kBytes = kQBytes + 2 * 2 * kTileBytes;  // Q + 2 buffers x (K, V)
+  // token-slice merge, reusing the K/V staging: [warp][16 rows][D + 2] floats
+  static constexpr int kCombineBytes = kWarps * 16 * (D + 2) * 4;
+  static_assert(kCombineBytes <= 2 * 2 * kTileBytes, "merge buffer exceeds the K/V staging");
+  static_assert((kRowBytes / 16) % 2 == 1, "ldmatrix rows must be an odd number of 16-byte units");
 };
 
+__device__ __forceinline__ uint32_t smem_addr(const void* ptr) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(ptr));
+}
+
+// 16-byte global -> shared copy; src_bytes 0 writes zeros (nothing is read)
+__device__ __forceinline__ void cp_async16(uint32_t dst, const void* src, uint32_t src_bytes) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst), "l"(src), "r"(src_bytes)
+               : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() {
+  asm volatile("cp.async.commit_group;" ::: "memory");
+}
+template <int N>
+__device__ __forceinline__ void cp_async_wait() {
+  asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
+
+__device__ __forceinline__ void ldsm_x4(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2,
+                                        uint32_t& r3) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0, %1, %2, %3}, [%4];"
+               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+               : "r"(addr)
+               : "memory");
+}
+__device__ __forceinline__ void ldsm_x4_t(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2,
+                                          uint32_t& r3) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0, %1, %2, %3}, [%4];"
+               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+               : "r"(addr)
+               : "memory");
+}
+
+template <typename T>
+__device__ __forceinline__ void mma16816(float (&c)[4], const uint32_t (&a)[4], uint32_t b0,
+                                         uint32_t b1) {
+  if constexpr (std::is_same<T, __nv_bfloat16>::value) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0, %1, %2, %3}, "
+        "{%4, %5, %6, %7}, {%8, %9}, {%0, %1, %2, %3};"
+        : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+  } else {
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0, %1, %2, %3}, "
+        "{%4, %5, %6, %7}, {%8, %9}, {%0, %1, %2, %3};"
+        : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+  }
+}
+
+template <typename T>
+__device__ __forceinline__ uint32_t pack_pair(float lo, float hi);
+template <>
+__device__ __forceinline__ uint32_t pack_pair<__nv_bfloat16>(float lo, float hi) {
+  __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
+  return *reinterpret_cast<uint32_t*>(&v);
+}
+template <>
+__device__ __forceinline__ uint32_t pack_pair<__half>(float lo, float hi) {
+  __half2 v = __floats2half2_rn(lo, hi);
+  return *reinterpret_cast<uint32_t*>(&v);
+}
+
 template <typename T, int D>
-__global__ void __launch_bounds__(kWarps * 32, 2) shared_range_kernel16(const SharedParams p) {
-  constexpr int kE = D / 32;              // output dims per lane
-  constexpr int kRowVecs = D / 8;         // 16-byte vectors per K/V row
-  constexpr int kPW = 8;                  // pairs per warp
-  extern __shared__ float4 smem4[];
-  float* sq = reinterpret_cast<float*>(smem4);
-  T* slab_all = reinterpret_cast<T*>(sq + Layout16<D>::kQFloats);
+__global__ void __launch_bounds__(kWarps * 32, 2) shared_range_mma_kernel(const SharedParams p) {
+  using L = LayoutMma<D>;
+  constexpr int kKSteps = D / 16;  // k16 steps over the head dim (S = Q K^T)
+  constexpr int kDTiles = D / 8;   // n8 tiles over the head dim (O)
+  constexpr int kRowVecs = D / 8;  // 16-byte vectors per row
+  extern __shared__ __align__(16) uint8_t smem[];
+  uint8_t* sq = smem;
+  uint8_t* skv = smem + L::kQBytes;  // [buffer][K, V][token][padded row]
 
   const int* c = p.chunks + blockIdx.x * 5;
   const int table_row = c[0], tok_begin = c[1], tok_end = c[2];
@@ -240,184 +309,243 @@ __global__ void __launch_bounds__(kWarps * 32, 2) shared_range_kernel16(const Sh
     if (tid == 0 && pairs != 0) raise_status(p.status, kStatusBadSequence);
     return;
   }
-  const int blocks = pairs <= kPW ? 1 : pairs <= 2 * kPW ? 2 : 4;  // pair blocks
-  const int splits = kWarps / blocks;                               // token splits
-  const int pb = warp % blocks, ts = warp / blocks;
-  const int pair0 = pb * kPW;
-  const int npairs = min(kPW, pairs - pair0);
+  const int tiles = pairs <= 16 ? 1 : 2;
+  const int slices = kWarps / tiles;  // 4 or 2 token slices per sub-tile
+  const int mt = warp % tiles, sl = warp / tiles;
+  const int slice_tokens = L::kTokens / slices;  // 16 or 32
+  const int g = lane >> 2, tig = lane & 3;
 
-  for (int e = tid; e < pairs * D; e += kWarps * 32) {
-    const int pair = e / D, d = e % D;
-    const int row = p.members[member_begin + pair / p.group];
-    const int qh = kvh * p.group + pair % p.group;
-    float x = 0.f;
-    if (row >= 0 && row < p.num_rows)
-      x = to_f32<T>(static_cast<const T*>(p.q)[row * p.q_rs + qh * p.q_hs + d]);
-    sq[e] = x * p.scale_log2;
+  // Q of every pair, in the input type (rows >= pairs stay zero)
+  for (int e = tid; e < kMaxPairs * kRowVecs; e += kWarps * 32) {
+    const int row = e / kRowVecs, v = e % kRowVecs;
+    uint32_t w[4] = {0, 0, 0, 0};
+    if (row < pairs) {
+      const int r = p.members[member_begin + row / p.group];
+      const int qh = kvh * p.group + row % p.group;
+      if (r >= 0 && r < p.num_rows) {
+        const T* src = static_cast<const T*>(p.q) + r * p.q_rs + qh * p.q_hs + v * 8;
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          T two[2] = {src[2 * i], src[2 * i + 1]};
+          w[i] = *reinterpret_cast<uint32_t*>(two);
+        }
+      }
+    }
+    *reinterpret_cast<uint4*>(sq + row * L::kRowBytes + v * 16) = make_uint4(w[0], w[1], w[2], w[3]);
   }
-  __syncthreads();
 
-  float m[kPW], l[kPW], o[kPW][kE];
-#pragma unroll
-  for (int i = 0; i < kPW; ++i) {
-    m[i] = -INFINITY;
-    l[i] = 0.f;
-#pragma unroll
-    for (int e = 0; e < kE; ++e) o[i][e] = 0.f;
-  }
-  T* slab = slab_all + warp * Layout16<D>::kSlabElems;
   const T* kbase = static_cast<const T*>(p.k) + kvh * p.k_hs;
   const T* vbase = static_cast<const T*>(p.v) + kvh * p.v_hs;
-
-  for (int t0 = tok_begin + ts * kSubTile; t0 < tok_end; t0 += splits * kSubTile) {
-    const int valid = min(kSubTile, tok_end - t0);
-    uint4 kreg[kRowVecs];
-#pragma unroll
-    for (int v = 0; v < kRowVecs; ++v) kreg[v] = make_uint4(0, 0, 0, 0);
-    if (lane < valid) {
-      const int pos = t0 + lane;
-      const int pg = pos / p.page;
-      int b = -1;
-      if (pg < p.width) {
-        b = p.tables[table_row * p.t_rs + pg];
-        if (b < 0 || b >= p.num_blocks) {
-          raise_status(p.status, kStatusBadBlock);
-          b = -1;
-        }
-      } else {
-        raise_status(p.status, kStatusBadLength);
-      }
-      uint4* srow = reinterpret_cast<uint4*>(slab + lane * D);
-      if (b >= 0) {
-        const T* kr = kbase + b * p.k_bs + (pos % p.page) * p.k_ts;
-        const T* vr = vbase + b * p.v_bs + (pos % p.page) * p.v_ts;
-#pragma unroll
-        for (int v = 0; v < kRowVecs; ++v) kreg[v] = ld_stream(kr + v * 8);
-#pragma unroll
-        for (int v = 0; v < kRowVecs; ++v) srow[v] = ld_stream(vr + v * 8);
-      } else {
-#pragma unroll
-        for (int v = 0; v < kRowVecs; ++v) srow[v] = make_uint4(0, 0, 0, 0);
-      }
-    }
-    __syncwarp();
-
-#pragma unroll
-    for (int i = 0; i < kPW; ++i) {
-      if (i >= npairs) break;  // warp-uniform
-      const float* qv = sq + (pair0 + i) * D;
-      float s = 0.f;
-#pragma unroll
-      for (int v = 0; v < kRowVecs; ++v) {
-        float kf[8];
-        unpack16<T>(kreg[v], kf);
-        const float4 a = *reinterpret_cast<const float4*>(qv + v * 8);
-        const float4 b = *reinterpret_cast<const float4*>(qv + v * 8 + 4);
-        s = fmaf(a.x, kf[0], s);
-        s = fmaf(a.y, kf[1], s);
-        s = fmaf(a.z, kf[2], s);
-        s = fmaf(a.w, kf[3], s);
-        s = fmaf(b.x, kf[4], s);
-        s = fmaf(b.y, kf[5], s);
-        s = fmaf(b.z, kf[6], s);
-        s = fmaf(b.w, kf[7], s);
-      }
-      s = lane < valid ? s : -INFINITY;
-      float mt = s;
-#pragma unroll
-      for (int off = 16; off > 0; off >>= 1) mt = fmaxf(mt, __shfl_xor_sync(kFullMask, mt, off));
-      const float m_new = fmaxf(m[i], mt);
-      const float corr = ex2(m[i] - m_new);
-      const float pr = lane < valid ? ex2(s - m_new) : 0.f;
-      float ps = pr;
-#pragma unroll
-      for (int off = 16; off > 0; off >>= 1) ps += __shfl_xor_sync(kFullMask, ps, off);
-      l[i] = l[i] * corr + ps;
-      m[i] = m_new;
-#pragma unroll
-      for (int e = 0; e < kE; ++e) o[i][e] *= corr;
-      for (int t = 0; t < valid; ++t) {
-        const float pt = __shfl_sync(kFullMask, pr, t);
-        const T* vr = slab + t * D + lane * kE;
-        if constexpr (kE == 4) {
-          const uint2 raw = *reinterpret_cast<const uint2*>(vr);
-          float v0, v1, v2, v3;
-          if constexpr (std::is_same<T, __nv_bfloat16>::value) {
-            bf16x2_to_f32(raw.x, v0, v1);
-            bf16x2_to_f32(raw.y, v2, v3);
-          } else {
-            f16x2_to_f32(raw.x, v0, v1);
-            f16x2_to_f32(raw.y, v2, v3);
+  auto tile_ptr = [&](int buf, int which) { return skv + (buf * 2 + which) * L::kTileBytes; };
+  auto load_tile = [&](int buf, int t0) {
+    for (int e = tid; e < 2 * L::kTokens * kRowVecs; e += kWarps * 32) {
+      const int which = e / (L::kTokens * kRowVecs);
+      const int idx = e % (L::kTokens * kRowVecs);
+      const int tok = idx / kRowVecs, v = idx % kRowVecs;
+      const int pos = t0 + tok;
+      const T* src = which ? vbase : kbase;  // any valid address when nothing is read
+      uint32_t bytes = 0;
+      if (pos < tok_end) {
+        const int pg = pos / p.page;
+        if (pg < p.width) {
+          const int b = p.tables[table_row * p.t_rs + pg];
+          if (b >= 0 && b < p.num_blocks) {
+            src = which ? vbase + b * p.v_bs + (pos % p.page) * p.v_ts + v * 8
+                        : kbase + b * p.k_bs + (pos % p.page) * p.k_ts + v * 8;
+            bytes = 16;
+          } else if (v == 0 && which == 0) {
+            raise_status(p.status, kStatusBadBlock);
           }
-          o[i][0] = fmaf(pt, v0, o[i][0]);
-          o[i][1] = fmaf(pt, v1, o[i][1]);
-          o[i][2] = fmaf(pt, v2, o[i][2]);
-          o[i][3] = fmaf(pt, v3, o[i][3]);
-        } else {
+        } else if (v == 0 && which == 0) {
+          raise_status(p.status, kStatusBadLength);
+        }
+      }
+      cp_async16(smem_addr(tile_ptr(buf, which) + tok * L::kRowBytes + v * 16), src, bytes);
+    }
+    cp_async_commit();
+  };
+  load_tile(0, tok_begin);
+  __syncthreads();  // Q staged
+
+  // Q fragments of this warp's M tile (matrix j = lane / 8: rows +8 for odd j,
+  // columns +8 for j >= 2)
+  uint32_t qa[kKSteps][4];
+  {
+    const int j = lane >> 3, r = lane & 7;
+    const uint8_t* base = sq + (mt * 16 + r + 8 * (j & 1)) * L::kRowBytes + 16 * (j >> 1);
 #pragma unroll
-          for (int e = 0; e < kE; ++e) o[i][e] = fmaf(pt, to_f32<T>(vr[e]), o[i][e]);
+    for (int ks = 0; ks < kKSteps; ++ks)
+      ldsm_x4(smem_addr(base + ks * 32), qa[ks][0], qa[ks][1], qa[ks][2], qa[ks][3]);
+  }
+
+  float o[kDTiles][4];
+#pragma unroll
+  for (int n = 0; n < kDTiles; ++n) o[n][0] = o[n][1] = o[n][2] = o[n][3] = 0.f;
+  float mrow[2] = {-INFINITY, -INFINITY}, lrow[2] = {0.f, 0.f};
+
+  int buf = 0;
+  for (int t0 = tok_begin; t0 < tok_end; t0 += L::kTokens, buf ^= 1) {
+    const bool more = t0 + L::kTokens < tok_end;
+    if (more) {
+      load_tile(buf ^ 1, t0 + L::kTokens);
+      cp_async_wait<1>();
+    } else {
+      cp_async_wait<0>();
+    }
+    __syncthreads();  // this sub-tile's K and V are in shared memory
+
+    const uint8_t* ktile = tile_ptr(buf, 0);
+    const uint8_t* vtile = tile_ptr(buf, 1);
+    const int tok0 = sl * slice_tokens;
+    float s[4][4];  // up to 4 n8 token tiles
+#pragma unroll
+    for (int j = 0; j < 4; ++j) s[j][0] = s[j][1] = s[j][2] = s[j][3] = 0.f;
+    {
+      // B fragments of K: matrix jj = lane / 8 -> token tile +(jj >> 1), dims +8 (jj & 1)
+      const int jj = lane >> 3, r = lane & 7;
+#pragma unroll
+      for (int ks = 0; ks < kKSteps; ++ks) {
+#pragma unroll
+        for (int j = 0; j < 4; j += 2) {
+          if (j * 8 >= slice_tokens) break;
+          const uint8_t* a = ktile + (tok0 + (j + (jj >> 1)) * 8 + r) * L::kRowBytes + ks * 32 +
+                             16 * (jj & 1);
+          uint32_t b0, b1, b2, b3;
+          ldsm_x4(smem_addr(a), b0, b1, b2, b3);
+          mma16816<T>(s[j], qa[ks], b0, b1);
+          mma16816<T>(s[j + 1], qa[ks], b2, b3);
         }
       }
     }
-    __syncwarp();  // the slab is rewritten by the next sub-tile
+    // scale, mask the tokens past the chunk, online softmax of rows g and g + 8
+    float mx[2] = {-INFINITY, -INFINITY};
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      if (j * 8 >= slice_tokens) break;
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const int tk = t0 + tok0 + j * 8 + 2 * tig + (e & 1);
+        s[j][e] = tk < tok_end ? s[j][e] * p.scale_log2 : -INFINITY;
+        mx[e >> 1] = fmaxf(mx[e >> 1], s[j][e]);
+      }
+    }
+    float corr[2], mref[2];
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      mx[h] = fmaxf(mx[h], __shfl_xor_sync(kFullMask, mx[h], 1));
+      mx[h] = fmaxf(mx[h], __shfl_xor_sync(kFullMask, mx[h], 2));
+      const float m_new = fmaxf(mrow[h], mx[h]);
+      mref[h] = m_new == -INFINITY ? 0.f : m_new;
+      corr[h] = ex2(mrow[h] - mref[h]);
+      mrow[h] = m_new;
+      lrow[h] *= corr[h];
+    }
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      if (j * 8 >= slice_tokens) break;
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        s[j][e] = ex2(s[j][e] - mref[e >> 1]);
+        lrow[e >> 1] += s[j][e];
+      }
+    }
+#pragma unroll
+    for (int n = 0; n < kDTiles; ++n) {
+      o[n][0] *= corr[0];
+      o[n][1] *= corr[0];
+      o[n][2] *= corr[1];
+      o[n][3] *= corr[1];
+    }
+    // O += P V over the slice's tokens, 16 at a time
+    {
+      const int jj = lane >> 3, r = lane & 7;
+#pragma unroll
+      for (int kk = 0; kk < 2; ++kk) {
+        if (kk * 16 >= slice_tokens) break;
+        uint32_t a[4];
+        a[0] = pack_pair<T>(s[2 * kk][0], s[2 * kk][1]);
+        a[1] = pack_pair<T>(s[2 * kk][2], s[2 * kk][3]);
+        a[2] = pack_pair<T>(s[2 * kk + 1][0], s[2 * kk + 1][1]);
+        a[3] = pack_pair<T>(s[2 * kk + 1][2], s[2 * kk + 1][3]);
+        // matrix jj: tokens +8 (jj & 1), dim tile +(jj >> 1)
+        const uint8_t* vrow = vtile + (tok0 + kk * 16 + 8 * (jj & 1) + r) * L::kRowBytes;
+#pragma unroll
+        for (int n = 0; n < kDTiles; n += 2) {
+          uint32_t b0, b1, b2, b3;
+          ldsm_x4_t(smem_addr(vrow + (n + (jj >> 1)) * 16), b0, b1, b2, b3);
+          mma16816<T>(o[n], a, b0, b1);
+          mma16816<T>(o[n + 1], a, b2, b3);
+        }
+      }
+    }
+    __syncthreads();  // every warp is done with this buffer before it is refilled
   }
 
-  // merge the token splits (shared memory reused: q and slabs are done)
+#pragma unroll
+  for (int h = 0; h < 2; ++h) {
+    lrow[h] += __shfl_xor_sync(kFullMask, lrow[h], 1);
+    lrow[h] += __shfl_xor_sync(kFullMask, lrow[h], 2);
+  }
+  // merge the token slices of each M tile (the K/V staging is free now)
+  float* cb = reinterpret_cast<float*>(skv);
+  {
+    float* mine = cb + warp * 16 * (D + 2);
+#pragma unroll
+    for (int n = 0; n < kDTiles; ++n) {
+      const int col = n * 8 + 2 * tig;
+      mine[g * (D + 2) + col] = o[n][0];
+      mine[g * (D + 2) + col + 1] = o[n][1];
+      mine[(g + 8) * (D + 2) + col] = o[n][2];
+      mine[(g + 8) * (D + 2) + col + 1] = o[n][3];
+    }
+    if (tig == 0) {
+      mine[g * (D + 2) + D] = mrow[0];
+      mine[g * (D + 2) + D + 1] = lrow[0];
+      mine[(g + 8) * (D + 2) + D] = mrow[1];
+      mine[(g + 8) * (D + 2) + D + 1] = lrow[1];
+    }
+  }
   __syncthreads();
-  float* cb = sq;  // [split][pair < kCombinePairs][D + 2]
-  if (splits > 1) {
+  if (sl != 0) return;
+  // warp (slice 0, tile mt): lane covers rows g, g + 8 and its columns
 #pragma unroll
-    for (int i = 0; i < kPW; ++i) {
-      if (i >= npairs) break;
-      float* st = cb + (ts * Layout16<D>::kCombinePairs + pair0 + i) * (D + 2);
-#pragma unroll
-      for (int e = 0; e < kE; ++e) st[lane * kE + e] = o[i][e];
-      if (lane == 0) {
-        st[D] = m[i];
-        st[D + 1] = l[i];
-      }
+  for (int h = 0; h < 2; ++h) {
+    const int row = g + 8 * h;
+    const int pair = mt * 16 + row;
+    float mxs = -INFINITY;
+    for (int k = 0; k < slices; ++k)
+      mxs = fmaxf(mxs, cb[((k * tiles + mt) * 16 + row) * (D + 2) + D]);
+    const float mref = mxs == -INFINITY ? 0.f : mxs;
+    float wk[kWarps];
+    float lsum = 0.f;
+    for (int k = 0; k < slices; ++k) {
+      const float* st = cb + ((k * tiles + mt) * 16 + row) * (D + 2);
+      wk[k] = ex2(st[D] - mref);
+      lsum += st[D + 1] * wk[k];
     }
-    __syncthreads();
-    if (ts != 0) return;
-#pragma unroll
-    for (int i = 0; i < kPW; ++i) {
-      if (i >= npairs) break;
-      float mx = -INFINITY;
-      for (int k = 0; k < splits; ++k)
-        mx = fmaxf(mx, cb[(k * Layout16<D>::kCombinePairs + pair0 + i) * (D + 2) + D]);
-      float ls = 0.f, acc[kE] = {};
-      for (int k = 0; k < splits; ++k) {
-        const float* st = cb + (k * Layout16<D>::kCombinePairs + pair0 + i) * (D + 2);
-        if (st[D + 1] <= 0.f) continue;
-        const float w = ex2(st[D] - mx);
-        ls += st[D + 1] * w;
-#pragma unroll
-        for (int e = 0; e < kE; ++e) acc[e] = fmaf(st[lane * kE + e], w, acc[e]);
-      }
-      m[i] = mx;
-      l[i] = ls;
-#pragma unroll
-      for (int e = 0; e < kE; ++e) o[i][e] = acc[e];
-    }
-  }
-
-#pragma unroll
-  for (int i = 0; i < kPW; ++i) {
-    if (i >= npairs) break;
-    const int pair = pair0 + i;
+    if (pair >= pairs) continue;
     const int slot = p.member_slots[member_begin + pair / p.group];
     if (slot < 0 || slot >= p.num_slots) {
-      if (lane == 0) raise_status(p.status, kStatusBadSequence);
+      if (tig == 0) raise_status(p.status, kStatusBadSequence);
       continue;
     }
     const int qh = kvh * p.group + pair % p.group;
-    float* dst = p.ws_o + (static_cast<int64_t>(slot) * p.hq + qh) * D + lane * kE;
+    float* dst = p.ws_o + (static_cast<int64_t>(slot) * p.hq + qh) * D;
 #pragma unroll
-    for (int e = 0; e < kE; ++e) dst[e] = o[i][e];
-    if (lane == 0) {
+    for (int n = 0; n < kDTiles; ++n) {
+#pragma unroll
+      for (int e = 0; e < 2; ++e) {
+        const int col = n * 8 + 2 * tig + e;
+        float acc = 0.f;
+        for (int k = 0; k < slices; ++k)
+          acc = fmaf(cb[((k * tiles + mt) * 16 + row) * (D + 2) + col], wk[k], acc);
+        dst[col] = acc;
+      }
+    }
+    if (tig == 0) {
       float* ml = p.ws_ml + (static_cast<int64_t>(slot) * p.hq + qh) * 2;
-      ml[0] = m[i];
-      ml[1] = l[i];
+      ml[0] = mxs;
+      ml[1] = lsum;
     }
   }
 }
@@ -478,12 +606,12 @@ int launch(const SharedParams& p, int num_chunks, const int32_t* row_slots,
     if (num_chunks > 0)
       shared_range_kernel<T, D><<<dim3(num_chunks, p.hkv), kWarps * 32, bytes, stream>>>(p);
   } else {
-    constexpr int bytes = Layout16<D>::kBytes;
+    constexpr int bytes = LayoutMma<D>::kBytes;
     static cudaError_t attr = cudaFuncSetAttribute(
-        shared_range_kernel16<T, D>, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+        shared_range_mma_kernel<T, D>, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
     if (attr != cudaSuccess) return static_cast<int>(attr);
     if (num_chunks > 0)
-      shared_range_kernel16<T, D><<<dim3(num_chunks, p.hkv), kWarps * 32, bytes, stream>>>(p);
+      shared_range_mma_kernel<T, D><<<dim3(num_chunks, p.hkv), kWarps * 32, bytes, stream>>>(p);
   }
   if (p.num_rows > 0)
     shared_merge_kernel<T, D><<<dim3(p.num_rows, ceil_div(p.hq, kWarps)), kWarps * 32, 0, stream>>>(
