@@ -133,7 +133,7 @@ def plan_arrays(tables, lengths, page: int, group: int, chunk_tokens: int = 256,
 
 
 def plan_shared_prefix(block_tables, context_lengths, page_size: int, num_q_heads: int,
-                       num_kv_heads: int, device, chunk_tokens: int = 256) -> SharedPrefixPlan:
+                       num_kv_heads: int, device, chunk_tokens: int = 512) -> SharedPrefixPlan:
     """Build the plan on the host (tables/lengths may be tensors on any
     device or numpy arrays) and upload it to ``device``."""
     tables = block_tables.cpu().numpy() if torch.is_tensor(block_tables) else np.asarray(block_tables)
