@@ -322,6 +322,24 @@ int rlt_rope_write_kv(const void* qkv, const int64_t* positions, const float* in
 int rlt_silu_mul(const void* gate_up, void* out, int32_t dtype, int32_t rows,
                  int32_t intermediate, int64_t in_stride, int64_t out_stride, void* stream);
 
+/* KV page transport for prefill/decode disaggregation: copy byte segments
+ * segments[i*3 + 0..2] = {source address, destination address, bytes}
+ * (device int64 array; addresses and sizes multiples of 16 bytes) on the
+ * stream's device. A destination on another GPU must be mapped in this
+ * process (rlt_enable_peer_access, or a CUDA-IPC mapping of the other
+ * process's pool); it is written with plain stores over NVLink.
+ * max_segment_bytes bounds the largest segment (it sizes the launch).
+ * Misaligned segments are skipped and raise RLT_STATUS_BAD_OFFSET.
+ * Replaces: the NIXL WRITE of vllm_rlt/pd/transport.py:114-133, whose
+ * segments come from kv_segments / partition_segments (:18-72). */
+int rlt_copy_segments(const int64_t* segments, int32_t num_segments, int64_t max_segment_bytes,
+                      int32_t* status, void* stream);
+
+/* Enable access from the current device to peer_device's memory (no-op if
+ * already enabled or if peer_device is the current device); RLT_E_DEVICE
+ * when the pair cannot use peer access. */
+int rlt_enable_peer_access(int32_t peer_device);
+
 #ifdef __cplusplus
 }
 #endif

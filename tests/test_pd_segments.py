@@ -1,0 +1,77 @@
+"""Prefill/decode KV transport host logic (CPU): the segment lists and their
+partition into transfers equal the reference's own outputs
+(tests/golden/pd_segments.json, made by tests/golden/make_pd_golden.py from
+vllm_rlt/pd/transport.py:18-72), and they cover exactly the valid tokens of
+every plane, layer, K and V."""
+
+from __future__ import annotations
+
+import json
+from pathlib import Path
+
+import pytest
+import torch
+
+from vllm_rlt_b200.pd import kv_segments, partition_segments, pool_info
+
+CASES = json.loads((Path(__file__).parent / "golden" / "pd_segments.json").read_text())
+
+
+@pytest.mark.parametrize("index", range(len(CASES)))
+def test_segments_match_reference(index):
+    case = CASES[index]
+    segments = [list(s) for s in kv_segments(case["info"], case["tables"], case["start"], case["end"])]
+    assert segments == case["segments"]
+    for limits in case["partitions"]:
+        parts = [[[list(x) for x in local], [list(x) for x in remote], size]
+                 for local, remote, size in partition_segments(
+                     [tuple(s) for s in segments], [tuple(s) for s in segments],
+                     limits["byte_limit"], limits["descriptor_limit"])]
+        assert parts == limits["parts"]
+        for local, _, size in parts:
+            assert size <= limits["byte_limit"] and len(local) <= limits["descriptor_limit"]
+
+
+@pytest.mark.parametrize("index", range(len(CASES)))
+def test_segments_cover_exactly_the_valid_tokens(index):
+    case = CASES[index]
+    info, tables, start, end = case["info"], case["tables"], case["start"], case["end"]
+    page = info["block_size"]
+    expected = set()
+    for table in tables:
+        for token in range(start, end):
+            for layer in range(info["num_layers"]):
+                for base in (info["key_ptr"], info["value_ptr"]):
+                    pos = (base + table[token // page] * info["block_bytes"]
+                           + layer * info["layer_bytes"] + (token % page) * info["token_bytes"])
+                    expected.add((pos, pos + info["token_bytes"]))
+    covered = set()
+    for address, size, _ in kv_segments(info, tables, start, end):
+        for pos in range(address, address + size, info["token_bytes"]):
+            covered.add((pos, pos + info["token_bytes"]))
+    assert covered == expected
+
+
+def test_invalid_ranges_and_blocks_raise():
+    case = CASES[0]
+    info, tables = case["info"], case["tables"]
+    for start, end in ((3, 3), (-1, 2), (5, 4)):
+        with pytest.raises(ValueError, match="invalid KV range"):
+            list(kv_segments(info, tables, start, end))
+    with pytest.raises(ValueError, match="exceeds allocation"):
+        list(kv_segments(info, tables, 0, len(tables[0]) * info["block_size"] + 1))
+    bad = [list(t) for t in tables]
+    bad[0][0] = info["num_blocks"]
+    with pytest.raises(ValueError, match="outside registered pool"):
+        list(kv_segments(info, bad, 0, 1))
+    with pytest.raises(ValueError, match="incompatible"):
+        list(partition_segments([(0, 16, 0)], [(0, 32, 0)], 64, 4))
+
+
+def test_pool_info_geometry():
+    k = torch.zeros(8, 3, 4, 2, 16, dtype=torch.bfloat16)
+    info = pool_info(k, torch.zeros_like(k), 4)
+    assert info["block_bytes"] == 3 * 4 * 2 * 16 * 2
+    assert info["layer_bytes"] == 4 * 2 * 16 * 2
+    assert info["token_bytes"] == 2 * 16 * 2
+    assert info["num_layers"] == 3 and info["num_blocks"] == 8

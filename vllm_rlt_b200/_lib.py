@@ -87,6 +87,8 @@ SIGNATURES = {
     "rlt_rms_norm": (_i32, [_p] * 4 + [_i32] * 3 + [_f32] + [_i64] * 3 + [_p]),
     "rlt_rope_write_kv": (_i32, [_p] * 9 + [_i32] * 7 + [_i64] * 8 + [_p]),
     "rlt_silu_mul": (_i32, [_p, _p, _i32, _i32, _i32, _i64, _i64, _p]),
+    "rlt_copy_segments": (_i32, [_p, _i32, _i64, _p, _p]),
+    "rlt_enable_peer_access": (_i32, [_i32]),
     "rlt_gather": (_i32, [_p, _p, _p, _i32, _i32, _i32, _i32, _i64, _i64, _p]),
     "rlt_scatter": (_i32, [_p, _p, _p, _i32, _i32, _i32, _i64, _i64, _p]),
 }
