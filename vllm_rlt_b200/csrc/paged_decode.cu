@@ -25,6 +25,8 @@
 //    an atomic per (row, head block) -- merges them, so there is no separate
 //    combine launch. The split plan is a function of the row's own length
 //    only, so results are batch-invariant.
+#include <atomic>
+
 #include "common.cuh"
 
 namespace rlt {
@@ -59,6 +61,9 @@ struct DecodeParams {
   float* ws_o;   // [rows, launch_splits, hq, head_dim] unnormalised acc
   float* ws_ml;  // [rows, launch_splits, hq, 2] (running max in log2 units, sum)
   int* counters;  // [rows, hq] finished-split counts (zeroed by the launcher)
+  const int* schedule;  // split launches: [rows + 1] first work item of each row (NULL: one
+                        // item per CTA, blockIdx = (row, head block), split)
+  int* work;            // split launches: next unclaimed work item
   float* lse;     // optional [rows, hq]: base-2 log-sum-exp of the scaled scores
                   // (max + log2(sum)); -inf for an empty row. NULL: not written
   int32_t* status;
@@ -161,9 +166,10 @@ __device__ __forceinline__ void merge_splits(const DecodeParams& p, int row, int
   }
 }
 
+// One work item: head block `rblock` of row `row`, split `split`.
 template <typename T, int D, int GC, bool ALIGNED>
-__global__ void __launch_bounds__(kDecodeWarps * 32, RLT_DECODE_MIN_BLOCKS)
-    paged_decode_kernel(const __grid_constant__ DecodeParams p) {
+__device__ __forceinline__ void decode_item(const DecodeParams& p, const int row, const int rblock,
+                                            const int split) {
   constexpr int VEC = Vec16<T>::kElems;
   constexpr int LPT = D / VEC;  // lanes per token row
   static_assert(LPT >= 4 && LPT <= 32 && (LPT & (LPT - 1)) == 0, "unsupported head_dim");
@@ -180,10 +186,7 @@ __global__ void __launch_bounds__(kDecodeWarps * 32, RLT_DECODE_MIN_BLOCKS)
   const int lane = threadIdx.x & 31;
   const int qchunks = p.group / GC;
   const int tasks_per_row = p.hkv * qchunks;
-  const int blocks_per_row = (tasks_per_row + kDecodeWarps - 1) / kDecodeWarps;
-  const int row = blockIdx.x / blocks_per_row;
-  const int task = (blockIdx.x - row * blocks_per_row) * kDecodeWarps + warp;
-  const int split = blockIdx.y;
+  const int task = rblock * kDecodeWarps + warp;
   // Warps past the row's last task stay alive for the CTA barrier of the
   // split merge; they compute nothing.
   const bool active = task < tasks_per_row;
@@ -455,8 +458,7 @@ __global__ void __launch_bounds__(kDecodeWarps * 32, RLT_DECODE_MIN_BLOCKS)
   __syncthreads();
   __shared__ int merge_here;
   if (threadIdx.x == 0) {
-    const int done = atomicAdd(p.counters + static_cast<int64_t>(row) * p.hq +
-                                   (blockIdx.x - row * blocks_per_row), 1);
+    const int done = atomicAdd(p.counters + static_cast<int64_t>(row) * p.hq + rblock, 1);
     merge_here = done == plan.count - 1;
   }
   __syncthreads();
@@ -464,6 +466,76 @@ __global__ void __launch_bounds__(kDecodeWarps * 32, RLT_DECODE_MIN_BLOCKS)
   __threadfence();
 #pragma unroll
   for (int c = 0; c < GC; ++c) merge_splits<T>(p, row, qh0 + c, plan.count, lane);
+}
+
+// Split launches run a fixed grid (one resident wave) whose CTAs claim work
+// items -- (row, split, head block), row-major, only splits that hold tokens
+// -- from a counter, after decode_schedule_kernel has laid the items out.
+// Launching one CTA per (row, head block, possible split) instead left most
+// CTAs with nothing to do on short rows, and their launches delayed the long
+// rows' splits. Single-split launches keep one CTA per (row, head block).
+template <typename T, int D, int GC, bool ALIGNED>
+__global__ void __launch_bounds__(kDecodeWarps * 32, RLT_DECODE_MIN_BLOCKS)
+    paged_decode_kernel(const __grid_constant__ DecodeParams p) {
+  const int tasks_per_row = p.hkv * (p.group / GC);
+  const int blocks_per_row = (tasks_per_row + kDecodeWarps - 1) / kDecodeWarps;
+  if (p.schedule == nullptr) {
+    const int row = blockIdx.x / blocks_per_row;
+    decode_item<T, D, GC, ALIGNED>(p, row, blockIdx.x - row * blocks_per_row, blockIdx.y);
+    return;
+  }
+  __shared__ int claimed;
+  const int total = p.schedule[p.rows];
+  for (;;) {
+    if (threadIdx.x == 0) claimed = atomicAdd(p.work, 1);
+    __syncthreads();
+    const int item = claimed;
+    __syncthreads();  // every thread has read it before thread 0 claims the next
+    if (item >= total) break;
+    int lo = 0, hi = p.rows - 1;  // the row: last r with schedule[r] <= item
+    while (lo < hi) {
+      const int mid = (lo + hi + 1) >> 1;
+      if (p.schedule[mid] <= item) lo = mid; else hi = mid - 1;
+    }
+    const int local = item - p.schedule[lo];
+    decode_item<T, D, GC, ALIGNED>(p, lo, local % blocks_per_row, local / blocks_per_row);
+  }
+}
+
+// Work items of a split launch: row r gets (its split count, 1 for an empty or
+// invalid row) x head blocks items starting at schedule[r]; schedule[rows] =
+// total. Also clears the merge counters and the claim counter. One CTA.
+constexpr int kScheduleThreads = 1024;
+__global__ void __launch_bounds__(kScheduleThreads) decode_schedule_kernel(
+    const __grid_constant__ DecodeParams p, int blocks_per_row, int* counters, int* schedule,
+    int* work) {
+  __shared__ int scan[kScheduleThreads];
+  const int tid = threadIdx.x;
+  const int64_t ncounters = static_cast<int64_t>(p.rows) * p.hq;
+  for (int64_t i = tid; i < ncounters; i += kScheduleThreads) counters[i] = 0;
+  if (tid == 0) *work = 0;
+  int carry = 0;
+  for (int base = 0; base < p.rows; base += kScheduleThreads) {
+    const int r = base + tid;
+    int items = 0;
+    if (r < p.rows) {
+      const int len = p.lengths[r];
+      const bool ok = len > 0 && static_cast<int64_t>(len) <= static_cast<int64_t>(p.width) * p.page;
+      items = (ok ? split_plan(len, p.launch_splits).count : 1) * blocks_per_row;
+    }
+    scan[tid] = items;
+    __syncthreads();
+    for (int off = 1; off < kScheduleThreads; off <<= 1) {  // inclusive scan
+      const int add = tid >= off ? scan[tid - off] : 0;
+      __syncthreads();
+      scan[tid] += add;
+      __syncthreads();
+    }
+    if (r < p.rows) schedule[r] = carry + scan[tid] - items;
+    carry += scan[kScheduleThreads - 1];
+    __syncthreads();
+  }
+  if (tid == 0) schedule[p.rows] = carry;
 }
 
 // Any head_dim <= 256, any alignment: one warp per (row, query head), dims
@@ -553,6 +625,20 @@ __global__ void prefill_rows_kernel(const int32_t* __restrict__ cu, const int32_
   row_len[i] = len > 0 ? len : 0;
 }
 
+// SM count of the current device (cached per device).
+int sm_count() {
+  static std::atomic<int> cache[64];
+  int device = 0;
+  if (cudaGetDevice(&device) != cudaSuccess || device < 0 || device >= 64) return 148;
+  int n = cache[device].load(std::memory_order_relaxed);
+  if (n == 0) {
+    if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, device) != cudaSuccess || n <= 0)
+      n = 148;
+    cache[device].store(n, std::memory_order_relaxed);
+  }
+  return n;
+}
+
 template <typename T, int D, int GC>
 cudaError_t launch_fast(const DecodeParams& p, cudaStream_t stream) {
   constexpr int VEC = Vec16<T>::kElems;
@@ -561,6 +647,13 @@ cudaError_t launch_fast(const DecodeParams& p, cudaStream_t stream) {
   const int tasks = p.hkv * (p.group / GC);
   const int blocks_per_row = (tasks + kDecodeWarps - 1) / kDecodeWarps;
   dim3 grid(static_cast<unsigned>(p.rows) * blocks_per_row, p.launch_splits);
+  if (p.schedule != nullptr) {
+    decode_schedule_kernel<<<1, kScheduleThreads, 0, stream>>>(
+        p, blocks_per_row, p.counters, const_cast<int*>(p.schedule), p.work);
+    const int64_t most = static_cast<int64_t>(p.rows) * blocks_per_row * p.launch_splits;
+    const int64_t wave = static_cast<int64_t>(sm_count()) * RLT_DECODE_MIN_BLOCKS;
+    grid = dim3(static_cast<unsigned>(most < wave ? most : wave), 1);
+  }
   if (p.page % TOK == 0)
     paged_decode_kernel<T, D, GC, true><<<grid, kDecodeWarps * 32, 0, stream>>>(p);
   else
@@ -633,9 +726,10 @@ struct DecodeArgs {
 
 size_t align16(size_t n) { return (n + 15) & ~static_cast<size_t>(15); }
 
-// Split scratch: [rows * hq] int counters | acc partials | (max, sum) partials.
+// Split scratch: [rows * hq] int merge counters | [rows + 1] schedule | claim
+// counter | acc partials | (max, sum) partials.
 size_t counter_bytes(int rows, int hq) {
-  return align16(static_cast<size_t>(rows) * hq * sizeof(int));
+  return align16((static_cast<size_t>(rows) * hq + rows + 2) * sizeof(int));
 }
 
 size_t split_bytes(int rows, int hq, int head_dim, int page, int width) {
@@ -698,12 +792,13 @@ DecodeParams make_params(const DecodeArgs& a, bool* fast) {
 
 int run(DecodeParams p, int32_t dtype, bool fast, void* split_ws, cudaStream_t s) {
   if (p.launch_splits > 1) {
-    // The split counters must start at zero on every call: one memset on the
-    // stream (allocation-free and capturable).
+    // The merge and claim counters and the work schedule are rebuilt on the
+    // stream by decode_schedule_kernel on every call (allocation-free and
+    // capturable).
     const size_t cbytes = counter_bytes(p.rows, p.hq);
-    const cudaError_t err = cudaMemsetAsync(split_ws, 0, cbytes, s);
-    if (err != cudaSuccess) return launch_status(err);
     p.counters = static_cast<int*>(split_ws);
+    p.schedule = p.counters + static_cast<size_t>(p.rows) * p.hq;
+    p.work = const_cast<int*>(p.schedule) + p.rows + 1;
     p.ws_o = reinterpret_cast<float*>(static_cast<char*>(split_ws) + cbytes);
     p.ws_ml = p.ws_o + static_cast<size_t>(p.rows) * p.launch_splits * p.hq * p.head_dim;
   }
