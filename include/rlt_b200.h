@@ -61,11 +61,12 @@ extern "C" {
 /* Library version (major*10000 + minor*100 + patch). */
 int rlt_version(void);
 
-/* Bytes of scratch rlt_paged_decode needs for this launch shape: one int
- * counter per (row, query head) -- cleared by every call with a memset on the
- * stream -- and fp32 split-KV partials (acc, running max, normaliser) for
- * every row, query head and split (a row of n tokens takes
- * min(ceil(n/256), 128) splits). 0 when no row can need more than one split. */
+/* Bytes of scratch rlt_paged_decode needs for this launch shape: int
+ * metadata -- one merge counter per (row, query head), the rows + 1 work
+ * schedule and a claim counter, all rebuilt on the stream by every call --
+ * and fp32 split-KV partials (acc, running max, normaliser) for every row,
+ * query head and split (a row of n tokens takes min(ceil(n/256), 128)
+ * splits). 0 when no row can need more than one split. */
 size_t rlt_paged_decode_workspace_bytes(int32_t num_rows, int32_t num_q_heads, int32_t head_dim,
                                         int32_t page_size, int32_t table_width);
 

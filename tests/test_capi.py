@@ -45,9 +45,11 @@ def test_host_only_entry_points_without_gpu():
     # no split can be needed when every row fits one split
     assert lib.rlt_paged_decode_workspace_bytes(8, 16, 128, 16, 16) == 0
     # graph width 4096 x page 16: up to 128 splits of fp32 (acc + max + sum),
-    # plus one int counter per (row, query head)
+    # after the int metadata -- one merge counter per (row, query head), the
+    # rows + 1 work schedule and the claim counter -- rounded to 16 bytes
+    meta = (256 * 16 + 256 + 2) * 4
     assert lib.rlt_paged_decode_workspace_bytes(256, 16, 128, 16, 4096) == (
-        256 * 16 * 4 + 256 * 128 * 16 * 130 * 4)
+        (meta + 15) // 16 * 16 + 256 * 128 * 16 * 130 * 4)
     assert lib.rlt_paged_prefill_workspace_bytes(0, 16, 128, 16, 64) == 0
 
 
