@@ -57,6 +57,7 @@ extern "C" {
 #define RLT_STATUS_BAD_SLOT 8
 #define RLT_STATUS_BAD_SEQUENCE 16
 #define RLT_STATUS_TIMEOUT 32 /* a bounded wait inside a tensor-core kernel gave up */
+#define RLT_STATUS_LAYOUT 64  /* a tensor-core kernel found its shared memory misaligned */
 
 /* Library version (major*10000 + minor*100 + patch). */
 int rlt_version(void);
@@ -142,10 +143,13 @@ int rlt_paged_prefill(const void* q, const void* key_cache, const void* value_ca
  * wheel makes the same choice internally. */
 int rlt_paged_prefill_uses_tensor_cores(int32_t dtype, int32_t head_dim, int32_t page_size);
 
-/* Diagnostics: choose the tensor-core prefill kernel for the process (3 =
- * warp-specialised two-tile kernel with P in TMEM, the default; 2 = the same
- * with P in shared memory; 1 = single-tile kernel); returns the previous
- * choice (any other value only queries). No counterpart in the reference. */
+/* Diagnostics: choose the tensor-core prefill kernel for the process (5 =
+ * warp-specialised two-tile kernel with P in TMEM whose softmax warpgroups
+ * hold a row's 128 scores in registers (setmaxnreg), the default; 4 = P in
+ * TMEM, each row's softmax split over two warps by key-column half; 3 = P in
+ * TMEM, one warp per 32 rows reading S twice; 2 = as 3 with P in shared
+ * memory; 1 = single-tile kernel); returns the previous choice (any other
+ * value only queries). No counterpart in the reference. */
 int rlt_prefill_tc_select(int32_t version);
 
 /* Decode attention that reads K/V pages shared by several rows once

@@ -109,13 +109,16 @@ def _with_version(version, fn):
 @pytest.mark.parametrize("dtype", ["bf16", "f16"])
 def test_each_tensor_core_kernel_vs_oracle(dtype, page):
     """Every tensor-core prefill kernel (1: single tile; 2: two tiles, P in
-    shared memory; 3: two tiles, P in TMEM) on long chunks that run many key
-    tiles, with ragged tails and a chunk shorter than one tile. Kernels 2 and
-    3 differ only in where P is held, so their outputs are bit-identical."""
+    shared memory; 3: two tiles, P in TMEM; 4: as 3 with each row's softmax
+    split over two warps by key-column half; 5: as 3 with the softmax
+    warpgroups' registers raised so a row's scores stay in registers for one
+    pass) on long chunks that run many key tiles, with ragged tails and a
+    chunk shorter than one tile. Kernels 2 and 3 differ only in where P is
+    held, so their outputs are bit-identical."""
     case = dict(page=page, seed=11, prompt=(1500, 2100, 90, 777), prefix=(0, 700, 30, 1),
                 chunk_cap=1100)
     outs = {}
-    for version in (1, 2, 3):
+    for version in (1, 2, 3, 4, 5):
         out, expected = _with_version(version, lambda: _prefix_reuse_case(dtype, **case))
         assert_close(to_numpy(out), expected, dtype, **FA4_TOLERANCE[dtype])
         outs[version] = out

@@ -38,6 +38,7 @@ STATUS_BITS = {
     8: "descriptor slot/depth/position outside the resident tables",
     16: "packed-prefill metadata inconsistent",
     32: "a bounded wait in a tensor-core kernel timed out",
+    64: "a tensor-core kernel found its shared memory misaligned",
 }
 
 _i32, _i64, _f32, _sz, _p = (

@@ -41,6 +41,7 @@ constexpr int kTileBytes = 2 * kHalfBytes;
 constexpr int kSmemBytes = 6 * kTileBytes + 1024;  // Q, K x2, V x2, P + alignment slack
 constexpr long long kWaitLimit = 100000000LL;      // cycles (~50 ms at 1.9 GHz)
 constexpr int32_t kStatusTimeout = 32;
+constexpr int32_t kStatusLayout = 64;  // dynamic shared memory base too far from 1024-byte alignment
 
 struct PrefillTcParams {
   CUtensorMap qmap;  // {D, Hq, tokens}, box {64, 1, 128}
@@ -424,6 +425,11 @@ __global__ void __launch_bounds__(kThreads, 1)
 //   warps 4-7  softmax of tile B
 //   warp 8     issues the tcgen05.mma (one elected thread)
 //   warp 9     issues the TMA loads (one elected thread)
+// Variants: kHalves = 2 doubles the softmax warps (two per 32 rows, one per
+// half of the key columns; MMA and producer become warps 16 and 17). kWide
+// keeps one softmax warp per 32 rows, adds idle warps 10-11 and moves
+// registers from warpgroup 2 to the softmax warpgroups so a row's 128 scores
+// stay in registers between the row max and the exponentials.
 // TMEM (512 columns): S_A [0,128), S_B [128,256), O_A [256,384), O_B [384,512).
 // Shared memory: Q_A, Q_B, K, V, P_A, P_B (32 KiB each, 128-byte swizzle).
 // Hand-offs are mbarriers only. The MMA issue order per key tile t is
@@ -433,36 +439,105 @@ __global__ void __launch_bounds__(kThreads, 1)
 // once both S(t) MMAs are done, V(t+1) once both PV(t) MMAs are done.
 
 constexpr int kPairRows = 2 * kTileM;
-constexpr int kPairThreads = 320;
 constexpr uint32_t kPairTmemCols = 512;
+// Threads of the two-tile kernel: 8 softmax warps per key-column half, the
+// MMA warp and the producer warp; the wide-register variant adds two idle
+// warps so that the MMA and producer warps form a whole warpgroup, which
+// gives its registers to the softmax warpgroups (setmaxnreg acts per
+// warpgroup).
+constexpr int pair_threads(int halves, bool wide) { return wide ? 12 * 32 : (8 * halves + 2) * 32; }
+// Register split of the wide variant: launched at 168 per thread (384
+// threads), the softmax warpgroups rise to 200 and the MMA/producer
+// warpgroup drops to 96: 256 x 200 + 128 x 96 = 63,488 <= 384 x 168 = 64,512.
+// (216/64 and 208/80 fit as well but spill more in the MMA and producer code.)
+constexpr int kWideLaunchRegs = 168;
+constexpr int kWideSoftRegs = 200;
+constexpr int kWideOtherRegs = 96;
+static_assert(256 * kWideSoftRegs + 128 * kWideOtherRegs <= 384 * kWideLaunchRegs,
+              "register split exceeds the launch allocation");
+
+// The two softmax warps that share 32 query rows (kHalves = 2) meet at named
+// barrier 1 + 4 x + quarter; the and-reduction carries a flag so that both
+// leave the key loop together.
+__device__ __forceinline__ bool pair_barrier_and(uint32_t id, bool pred) {
+  uint32_t all;
+  asm volatile(
+      "{\n\t.reg .pred pi, po;\n\t"
+      "setp.ne.u32 pi, %1, 0;\n\t"
+      "bar.red.and.pred po, %2, 64, pi;\n\t"
+      "selp.u32 %0, 1, 0, po;\n\t}"
+      : "=r"(all)
+      : "r"(static_cast<uint32_t>(pred)), "r"(id)
+      : "memory");
+  return all != 0;
+}
+
+__device__ __forceinline__ void pair_barrier(uint32_t id) {
+  asm volatile("bar.sync %0, 64;" ::"r"(id) : "memory");
+}
 // K(t), V(t) stream through a ring of 32 KiB slots: item 2t = K(t), 2t+1 =
 // V(t), slot = item % slots. With P in TMEM (kPTmem) the two P buffers of
 // shared memory go to the ring instead: 5 slots rather than 3.
+constexpr int kMaxRingSlots = 5;
+// Barriers, flags and the softmax pair exchange, after the tiles in dynamic
+// shared memory (the kernel has no static shared memory).
+struct PairShared {
+  uint64_t bar_q, bar_full[kMaxRingSlots], bar_empty[kMaxRingSlots];
+  uint64_t bar_s[2], bar_p[2], bar_pv[2];
+  uint32_t tmem_base;
+  int tile_seq, tile_m0, abort_flag;
+  float pair_red[2 * 2 * kTileM];  // row max, then row sum, per (tile, half, row)
+};
+constexpr int kMaxSmem = 227 * 1024;
 template <bool kPTmem>
 struct PairLayout {
   static constexpr int kSlots = kPTmem ? 5 : 3;
   static constexpr int kPBuffers = kPTmem ? 0 : 2;
-  static constexpr int kSmemBytes = (2 + kPBuffers + kSlots) * kTileBytes + 1024;
+  static constexpr int kTileRegion = (2 + kPBuffers + kSlots) * kTileBytes;
+  // all a CTA may have: the tiles need a 1024-byte aligned start, and the
+  // allocation's base is aligned at least that well in practice; the kernel
+  // checks that the slack covers the distance it must skip
+  static constexpr int kSmemBytes = kMaxSmem;
+  static constexpr int kSlack = kSmemBytes - kTileRegion - static_cast<int>(sizeof(PairShared));
 };
-constexpr int kMaxRingSlots = 5;
-static_assert(PairLayout<true>::kSmemBytes <= 227 * 1024 && PairLayout<false>::kSmemBytes <= 227 * 1024,
+static_assert(PairLayout<true>::kSlack >= 0 && PairLayout<false>::kSlack >= 0,
               "shared memory per CTA");
 
-template <typename T, bool kPTmem>
-__global__ void __launch_bounds__(kPairThreads, 1)
+template <typename T, bool kPTmem, int kHalves, bool kWide>
+__global__ void __launch_bounds__(pair_threads(kHalves, kWide), 1)
     paged_prefill_tc2_kernel(const __grid_constant__ PrefillTcParams p) {
+  static_assert(kHalves == 1 || (kHalves == 2 && kPTmem), "split softmax needs P in TMEM");
+  static_assert(!kWide || (kHalves == 1 && kPTmem), "wide registers: one warp per row set");
   constexpr int kRingSlots = PairLayout<kPTmem>::kSlots;
+  constexpr int kSoftWarps = 8 * kHalves;
+  constexpr int kMmaWarp = kSoftWarps;
+  constexpr int kProducerWarp = kSoftWarps + 1;
+  constexpr int kCols = kTileN / kHalves;     // key columns of S per softmax warp
+  constexpr int kOCols = kHeadDim / kHalves;  // O columns each softmax warp rescales and stores
+  // declared without an alignment the compiler could fold the check below into
   extern __shared__ uint8_t smem_raw[];
-  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
-                                             ~static_cast<uintptr_t>(1023));
+  const uintptr_t raw = reinterpret_cast<uintptr_t>(smem_raw);
+  const uintptr_t skip = ((raw + 1023) & ~static_cast<uintptr_t>(1023)) - raw;
+  if (skip > static_cast<uintptr_t>(PairLayout<kPTmem>::kSlack)) {  // uniform: no access yet
+    if (threadIdx.x == 0) raise_status(p.status, kStatusLayout);
+    return;
+  }
+  uint8_t* smem = smem_raw + skip;
   uint8_t* sQ[2] = {smem, smem + kTileBytes};
   // P_x (shared-memory variant only) at smem + (2 + x) * kTileBytes
   uint8_t* ring = smem + (2 + PairLayout<kPTmem>::kPBuffers) * kTileBytes;
-
-  __shared__ __align__(8) uint64_t bar_q, bar_full[kMaxRingSlots], bar_empty[kMaxRingSlots];
-  __shared__ __align__(8) uint64_t bar_s[2], bar_p[2], bar_pv[2];
-  __shared__ uint32_t tmem_base_sh;
-  __shared__ int tile_seq, tile_m0, abort_flag;
+  PairShared& sh = *reinterpret_cast<PairShared*>(smem + PairLayout<kPTmem>::kTileRegion);
+  uint64_t& bar_q = sh.bar_q;
+  uint64_t* bar_full = sh.bar_full;
+  uint64_t* bar_empty = sh.bar_empty;
+  uint64_t* bar_s = sh.bar_s;
+  uint64_t* bar_p = sh.bar_p;
+  uint64_t* bar_pv = sh.bar_pv;
+  uint32_t& tmem_base_sh = sh.tmem_base;
+  int& tile_seq = sh.tile_seq;
+  int& tile_m0 = sh.tile_m0;
+  int& abort_flag = sh.abort_flag;
+  float* pair_red = sh.pair_red;
 
   const int tid = threadIdx.x;
   const int warp = tid >> 5;
@@ -480,7 +555,7 @@ __global__ void __launch_bounds__(kPairThreads, 1)
     }
     for (int x = 0; x < 2; ++x) {
       tc::mbar_init(&bar_s[x], 1);
-      tc::mbar_init(&bar_p[x], kTileM / 32);  // one arrival per softmax warp
+      tc::mbar_init(&bar_p[x], kSoftWarps / 2);  // one arrival per softmax warp
       tc::mbar_init(&bar_pv[x], 1);
     }
     tc::fence_mbar_init();
@@ -512,7 +587,7 @@ __global__ void __launch_bounds__(kPairThreads, 1)
   }
   const bool active = seq >= 0 && n_tiles > 0;
 
-  if (active && warp == 9) {
+  auto producer_role = [&]() {
     // ---------------- TMA producer. The warp's lanes fetch the block ids of
     // a key tile together (lane j: page j) one tile ahead of its copies, so
     // no table read sits between two copies; lane 0 issues the copies.
@@ -582,7 +657,8 @@ __global__ void __launch_bounds__(kPairThreads, 1)
         tc::mbar_wait(&bar_full[i % kRingSlots], (i / kRingSlots) & 1, kWaitLimit);
       tc::mbar_wait(&bar_q, 0, kWaitLimit);
     }
-  } else if (active && warp == 8) {
+  };
+  auto mma_role = [&]() {
     // ---------------- MMA issuer
     if (lane == 0) {
       constexpr uint32_t idesc_qk = tc::idesc_f16(Fmt<T>::value, kTileM, kTileN, 0);
@@ -621,8 +697,11 @@ __global__ void __launch_bounds__(kPairThreads, 1)
           const uint64_t bdesc = tc::desc64(vb + ks * (2048 >> 4), v_hi);
           const uint32_t acc = ks > 0 ? 1u : accumulate;
           if constexpr (kPTmem) {
-            // P_x over the first 64 columns of S_x: 8 columns (16 keys) per step
-            tc::mma_f16_ts(tmem + 2 * kTileN + x * kHeadDim, tmem + x * kTileN + ks * 8, bdesc,
+            // P_x over S_x's columns, 8 columns (16 keys) per step: the first
+            // 64 columns, or with the split softmax each half's P at the start
+            // of its own 64 S columns ([0, 32) and [64, 96))
+            const uint32_t pcol = ks * 8 + (kHalves == 2 && ks >= 4 ? 32 : 0);
+            tc::mma_f16_ts(tmem + 2 * kTileN + x * kHeadDim, tmem + x * kTileN + pcol, bdesc,
                            idesc_pv, acc);
           } else {
             const uint32_t off = ((ks >> 2) * kHalfBytes + (ks & 3) * 32) >> 4;
@@ -646,10 +725,13 @@ __global__ void __launch_bounds__(kPairThreads, 1)
       // interleaved four k-steps at a time: a run of eight MMAs of one
       // B-operand major-ness followed by eight of the other costs the tensor
       // core about 30 cycles per MMA, runs of four or less cost nothing.
+      // With P in TMEM, bar_pv is committed after the last PV only: S_x(t+1)
+      // follows PV_x(t), and a commit tracks every earlier MMA of this
+      // thread, so S_x(t+1) ready already means PV_x(t) is done.
       auto after_p = [&](int x, int v_slot, int k_slot, bool more, uint32_t accumulate) {
         if constexpr (kPTmem) {
           pv_steps(x, v_slot, 0, 8, accumulate);
-          commit_pv(x);
+          if (!more) commit_pv(x);
           if (more) {
             s_steps(x, k_slot, 0, 8);
             commit_s(x);
@@ -681,12 +763,16 @@ __global__ void __launch_bounds__(kPairThreads, 1)
         const int k_next = v_slot + 1 == kRingSlots ? 0 : v_slot + 1;
         const bool more = t + 1 < n_tiles;
         const uint32_t accumulate = t > 0 ? 1u : 0u;
-        ok = tc::mbar_wait(&bar_p[0], t & 1, kWaitLimit) && wait_item(2 * t + 1) &&
-             (!more || wait_item(2 * t + 2));
+        // the ring items first: they landed long ago, and testing them while
+        // the softmax of tile A still runs keeps them off the path from P_A
+        // to the MMAs. The P barriers are polled (test_wait, never
+        // suspended): this one thread's wake-up is on the critical path.
+        ok = wait_item(2 * t + 1) && (!more || wait_item(2 * t + 2)) &&
+             tc::mbar_poll(&bar_p[0], t & 1, kWaitLimit);
         if (!ok) break;
         tc::tc_fence_after();
         after_p(0, v_slot, k_next, more, accumulate);
-        ok = tc::mbar_wait(&bar_p[1], t & 1, kWaitLimit);
+        ok = tc::mbar_poll(&bar_p[1], t & 1, kWaitLimit);
         if (!ok) break;
         tc::tc_fence_after();
         after_p(1, v_slot, k_next, more, accumulate);
@@ -703,82 +789,71 @@ __global__ void __launch_bounds__(kPairThreads, 1)
         }
       }
     }
-  } else if (active && warp < 8) {
-    // ---------------- softmax of tile x, one query row per thread
-    const int x = warp >> 2;
-    const int r = tid & (kTileM - 1);
-    const uint32_t lane_base = static_cast<uint32_t>((warp & 3) * 32) << 16;
-    const uint32_t s_tmem = tmem + x * kTileN + lane_base;
-    const uint32_t o_tmem = tmem + 2 * kTileN + x * kHeadDim + lane_base;
+  };
+  auto softmax_role = [&]() {
+    // ---------------- softmax of tile x, one query row per thread; with
+    // kHalves = 2 two warps share the rows, one per half of the key columns
+    const int x = warp / (4 * kHalves);
+    const int h = kHalves == 2 ? (warp >> 2) & 1 : 0;
+    const int quarter = warp & 3;  // TMEM lanes [32 quarter, 32 quarter + 32)
+    const int r = quarter * 32 + lane;
+    const uint32_t pair_id = 1 + x * 4 + quarter;
+    const uint32_t lane_base = static_cast<uint32_t>(quarter * 32) << 16;
+    const uint32_t s_tmem = tmem + x * kTileN + h * kCols + lane_base;
+    const uint32_t o_tmem = tmem + 2 * kTileN + x * kHeadDim + h * kOCols + lane_base;
     const int qi = m0 + x * kTileM + r;
     const int row_limit = min(ctx - qlen + qi, ctx - 1);
     float m_used = -INFINITY;
     float l_sum = 0.f;
     int t = 0;
     for (; t < n_tiles; ++t) {
-      // loop exits are warp-uniform: the next statement is a warp-collective
-      // tcgen05.ld
-      const bool ready = *aborted == 0 && tc::mbar_wait(&bar_s[x], t & 1, kWaitLimit);
-      if (!__all_sync(kFullMask, ready)) {
+      // loop exits are warp-uniform (pair-uniform with kHalves = 2): the
+      // next statement is a warp-collective tcgen05.ld
+      const bool ready = __all_sync(
+          kFullMask, *aborted == 0 && tc::mbar_wait(&bar_s[x], t & 1, kWaitLimit));
+      if (kHalves == 1 && !ready) {
         *aborted = 1;
         break;
       }
       tc::tc_fence_after();
-      const int n0 = t * kTileN;
-      // Ten warps put three on one SM sub-partition, which caps a thread at
-      // 168 registers: S is read from TMEM twice, 64 columns per wait.
+      const int n0 = t * kTileN + h * kCols;  // this warp's first key
       // keys past the causal limit somewhere in the warp (warp-uniform, so the
       // TMEM collectives below never sit under a divergent branch)
-      const bool diagonal = __any_sync(kFullMask, n0 + kTileN - 1 > row_limit);
-      // Row max, 64 columns per TMEM wait. The pass exists in two
-      // instantiations, with and without the causal mask, chosen by one
-      // warp-uniform branch: a mask test inside the unrolled loops was
-      // predicated into every key tile, not just the diagonal ones.
-      auto row_max = [&](auto masked) {
-        constexpr bool kMasked = decltype(masked)::value;
-        float m = -INFINITY;
+      const bool diagonal = __any_sync(kFullMask, n0 + kCols - 1 > row_limit);
+      if constexpr (kWide) {
+        // One pass: the row's 128 scores stay in registers from the TMEM
+        // load to the P store. Masked scores become -inf, whose exponential
+        // is 0, so the probabilities need no mask of their own.
+        uint32_t sr[4][32];
 #pragma unroll
-        for (int hb = 0; hb < 2; ++hb) {
-          uint32_t sr[2][32];
-          tc::tmem_ld32(s_tmem + hb * 64, sr[0]);
-          tc::tmem_ld32(s_tmem + hb * 64 + 32, sr[1]);
-          tc::tmem_ld_wait(sr[0]);
-          tc::tmem_ld_wait(sr[1]);
-          if constexpr (kMasked) {
+        for (int c = 0; c < 4; ++c) tc::tmem_ld32(s_tmem + c * 32, sr[c]);
 #pragma unroll
-            for (int c = 0; c < 2; ++c)
+        for (int c = 0; c < 4; ++c) tc::tmem_ld_wait(sr[c]);
+        if (diagonal) {
 #pragma unroll
-              for (int j = 0; j < 32; ++j)
-                if (n0 + hb * 64 + c * 32 + j > row_limit) sr[c][j] = __float_as_uint(-INFINITY);
-          }
+          for (int c = 0; c < 4; ++c)
 #pragma unroll
-          for (int c = 0; c < 2; ++c)
-#pragma unroll
-            for (int j = 0; j < 32; j += 2)
-              m = max3(m, __uint_as_float(sr[c][j]), __uint_as_float(sr[c][j + 1]));
+            for (int j = 0; j < 32; ++j)
+              if (n0 + c * 32 + j > row_limit) sr[c][j] = __float_as_uint(-INFINITY);
         }
-        return m;
-      };
-      float mx;
-      if (diagonal)
-        mx = row_max(std::true_type{});
-      else
-        mx = row_max(std::false_type{});
-      const float m_new = fmaxf(m_used, mx * p.scale_log2);
-      float factor = 1.f;
-      if (m_new > m_used + 8.f) {
-        factor = ex2(m_used - m_new);
-        m_used = m_new;
-      }
-      const float neg_mref = m_used == -INFINITY ? 0.f : -m_used;
-      // PV(t-1) must be done: it read P_x and it wrote O_x.
-      if (t > 0) {
-        if (!__all_sync(kFullMask, tc::mbar_wait(&bar_pv[x], (t - 1) & 1, kWaitLimit))) {
-          *aborted = 1;
-          break;
+        float mc[4];
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+          mc[c] = -INFINITY;
+#pragma unroll
+          for (int j = 0; j < 32; j += 2)
+            mc[c] = max3(mc[c], __uint_as_float(sr[c][j]), __uint_as_float(sr[c][j + 1]));
         }
-        tc::tc_fence_after();
-        if (__any_sync(kFullMask, factor != 1.f)) {  // warp-collective TMEM access
+        const float mx = fmaxf(fmaxf(mc[0], mc[1]), fmaxf(mc[2], mc[3]));
+        const float m_new = fmaxf(m_used, mx * p.scale_log2);
+        float factor = 1.f;
+        if (m_new > m_used + 8.f) {
+          factor = ex2(m_used - m_new);
+          m_used = m_new;
+        }
+        const float neg_mref = m_used == -INFINITY ? 0.f : -m_used;
+        // PV_x(t-1) is done (S_x(t) was issued after it): rescale O_x
+        if (t > 0 && __any_sync(kFullMask, factor != 1.f)) {
 #pragma unroll
           for (int c = 0; c < 4; ++c) {
             uint32_t o[32];
@@ -790,61 +865,163 @@ __global__ void __launch_bounds__(kPairThreads, 1)
           }
           tc::tmem_st_wait();
         }
-      }
-      // probabilities p = 2^(s * scale_log2 - m) -> P_x, row sum. Every
-      // exponential runs on the MUFU unit: a polynomial on the FMA pipe needs
-      // integer and min/max work on the ALU pipe, which the row max and the
-      // P conversion already keep busy, and measured slower at every split
-      // tried (1/8 to 1/2 of the columns). Arguments and sums use packed
-      // fp32x2 ops.
-      const uint64_t scale2 = pk2(p.scale_log2, p.scale_log2);
-      const uint64_t neg2 = pk2(neg_mref, neg_mref);
-      auto probabilities = [&](auto masked) {
-        constexpr bool kMasked = decltype(masked)::value;
+        const uint64_t scale2 = pk2(p.scale_log2, p.scale_log2);
+        const uint64_t neg2 = pk2(neg_mref, neg_mref);
         uint64_t psum2 = pk2(0.f, 0.f);
 #pragma unroll
-        for (int cc = 0; cc < 4; ++cc) {  // 32-column chunks
-          uint32_t sr[32];
-          tc::tmem_ld32(s_tmem + cc * 32, sr);
-          tc::tmem_ld_wait(sr);
+        for (int c = 0; c < 4; ++c) {
           uint32_t packed[16];
 #pragma unroll
           for (int j = 0; j < 32; j += 2) {
             const uint64_t arg =
-                fma2(pk2(__uint_as_float(sr[j]), __uint_as_float(sr[j + 1])), scale2, neg2);
+                fma2(pk2(__uint_as_float(sr[c][j]), __uint_as_float(sr[c][j + 1])), scale2, neg2);
             float p0, p1;
             upk2(arg, p0, p1);
             p0 = ex2(p0);
             p1 = ex2(p1);
-            if constexpr (kMasked) {
-              const int key = n0 + cc * 32 + j;
-              p0 = key <= row_limit ? p0 : 0.f;
-              p1 = key + 1 <= row_limit ? p1 : 0.f;
-            }
             psum2 = add2(psum2, pk2(p0, p1));
             packed[j / 2] = pack2<T>(p0, p1);
           }
-          if constexpr (kPTmem) {
-            // P columns [16 cc, 16 cc + 16) of S_x: S columns this thread already read
-            tc::tmem_st16(s_tmem + cc * 16, packed);
-          } else {
-            uint8_t* base = smem + (2 + x) * kTileBytes + (cc >> 1) * kHalfBytes;  // P_x
-#pragma unroll
-            for (int v = 0; v < 4; ++v)
-              *reinterpret_cast<uint4*>(base + sw128(r, (cc & 1) * 4 + v)) =
-                  make_uint4(packed[4 * v], packed[4 * v + 1], packed[4 * v + 2], packed[4 * v + 3]);
-          }
+          tc::tmem_st16(s_tmem + c * 16, packed);  // S columns already in registers
         }
         float lo, hi;
         upk2(psum2, lo, hi);
-        return lo + hi;
-      };
-      float psum;
-      if (diagonal)
-        psum = probabilities(std::true_type{});
-      else
-        psum = probabilities(std::false_type{});
-      l_sum = l_sum * factor + psum;
+        l_sum = l_sum * factor + (lo + hi);
+      } else {
+        // Row max, 64 columns per TMEM wait. The pass exists in two
+        // instantiations, with and without the causal mask, chosen by one
+        // warp-uniform branch: a mask test inside the unrolled loops was
+        // predicated into every key tile, not just the diagonal ones.
+        auto row_max = [&](auto masked) {
+          constexpr bool kMasked = decltype(masked)::value;
+          float m = -INFINITY;
+  #pragma unroll
+          for (int hb = 0; hb < kCols / 64; ++hb) {
+            uint32_t sr[2][32];
+            tc::tmem_ld32(s_tmem + hb * 64, sr[0]);
+            tc::tmem_ld32(s_tmem + hb * 64 + 32, sr[1]);
+            tc::tmem_ld_wait(sr[0]);
+            tc::tmem_ld_wait(sr[1]);
+            if constexpr (kMasked) {
+  #pragma unroll
+              for (int c = 0; c < 2; ++c)
+  #pragma unroll
+                for (int j = 0; j < 32; ++j)
+                  if (n0 + hb * 64 + c * 32 + j > row_limit) sr[c][j] = __float_as_uint(-INFINITY);
+            }
+  #pragma unroll
+            for (int c = 0; c < 2; ++c)
+  #pragma unroll
+              for (int j = 0; j < 32; j += 2)
+                m = max3(m, __uint_as_float(sr[c][j]), __uint_as_float(sr[c][j + 1]));
+          }
+          return m;
+        };
+        float mx = -INFINITY;
+        if (ready) {
+          if (diagonal)
+            mx = row_max(std::true_type{});
+          else
+            mx = row_max(std::false_type{});
+        }
+        if constexpr (kHalves == 2) {
+          // both halves take the larger maximum (fmaxf is exact and symmetric,
+          // so the two warps hold the same base, factor and P scale)
+          pair_red[(x * 2 + h) * kTileM + r] = mx;
+          if (!pair_barrier_and(pair_id, ready)) {
+            *aborted = 1;
+            break;
+          }
+          mx = fmaxf(mx, pair_red[(x * 2 + (h ^ 1)) * kTileM + r]);
+        }
+        const float m_new = fmaxf(m_used, mx * p.scale_log2);
+        float factor = 1.f;
+        if (m_new > m_used + 8.f) {
+          factor = ex2(m_used - m_new);
+          m_used = m_new;
+        }
+        const float neg_mref = m_used == -INFINITY ? 0.f : -m_used;
+        // PV(t-1) must be done: it read P_x and it wrote O_x. With P in TMEM
+        // the S_x(t) completion seen above implies it (S_x(t) was issued after
+        // PV_x(t-1)). A timed-out wait marks the call aborted and skips the
+        // rescale; the next key tile's readiness test then ends the loop (for
+        // both warps of a pair).
+        if (t > 0) {
+          if (!kPTmem &&
+              !__all_sync(kFullMask, tc::mbar_wait(&bar_pv[x], (t - 1) & 1, kWaitLimit))) {
+            *aborted = 1;
+          } else {
+            tc::tc_fence_after();
+            if (__any_sync(kFullMask, factor != 1.f)) {  // warp-collective TMEM access
+  #pragma unroll
+              for (int c = 0; c < kOCols / 32; ++c) {
+                uint32_t o[32];
+                tc::tmem_ld32(o_tmem + c * 32, o);
+                tc::tmem_ld_wait(o);
+  #pragma unroll
+                for (int j = 0; j < 32; ++j) o[j] = __float_as_uint(__uint_as_float(o[j]) * factor);
+                tc::tmem_st32(o_tmem + c * 32, o);
+              }
+              tc::tmem_st_wait();
+            }
+          }
+        }
+        // probabilities p = 2^(s * scale_log2 - m) -> P_x, row sum. Every
+        // exponential runs on the MUFU unit: a polynomial on the FMA pipe needs
+        // integer and min/max work on the ALU pipe, which the row max and the
+        // P conversion already keep busy, and measured slower at every split
+        // tried (1/8 to 1/2 of the columns). Arguments and sums use packed
+        // fp32x2 ops.
+        const uint64_t scale2 = pk2(p.scale_log2, p.scale_log2);
+        const uint64_t neg2 = pk2(neg_mref, neg_mref);
+        auto probabilities = [&](auto masked) {
+          constexpr bool kMasked = decltype(masked)::value;
+          uint64_t psum2 = pk2(0.f, 0.f);
+  #pragma unroll
+          for (int cc = 0; cc < kCols / 32; ++cc) {  // 32-column chunks
+            uint32_t sr[32];
+            tc::tmem_ld32(s_tmem + cc * 32, sr);
+            tc::tmem_ld_wait(sr);
+            uint32_t packed[16];
+  #pragma unroll
+            for (int j = 0; j < 32; j += 2) {
+              const uint64_t arg =
+                  fma2(pk2(__uint_as_float(sr[j]), __uint_as_float(sr[j + 1])), scale2, neg2);
+              float p0, p1;
+              upk2(arg, p0, p1);
+              p0 = ex2(p0);
+              p1 = ex2(p1);
+              if constexpr (kMasked) {
+                const int key = n0 + cc * 32 + j;
+                p0 = key <= row_limit ? p0 : 0.f;
+                p1 = key + 1 <= row_limit ? p1 : 0.f;
+              }
+              psum2 = add2(psum2, pk2(p0, p1));
+              packed[j / 2] = pack2<T>(p0, p1);
+            }
+            if constexpr (kPTmem) {
+              // P columns [16 cc, 16 cc + 16) of this warp's S columns: ones
+              // this thread already read
+              tc::tmem_st16(s_tmem + cc * 16, packed);
+            } else {
+              uint8_t* base = smem + (2 + x) * kTileBytes + (cc >> 1) * kHalfBytes;  // P_x
+  #pragma unroll
+              for (int v = 0; v < 4; ++v)
+                *reinterpret_cast<uint4*>(base + sw128(r, (cc & 1) * 4 + v)) =
+                    make_uint4(packed[4 * v], packed[4 * v + 1], packed[4 * v + 2], packed[4 * v + 3]);
+            }
+          }
+          float lo, hi;
+          upk2(psum2, lo, hi);
+          return lo + hi;
+        };
+        float psum;
+        if (diagonal)
+          psum = probabilities(std::true_type{});
+        else
+          psum = probabilities(std::false_type{});
+        l_sum = l_sum * factor + psum;
+      }
       if constexpr (kPTmem)
         tc::tmem_st_wait();
       else
@@ -854,17 +1031,27 @@ __global__ void __launch_bounds__(kPairThreads, 1)
       if (lane == 0) tc::mbar_arrive(&bar_p[x]);
     }
     if (t == n_tiles) {
-      if (!__all_sync(kFullMask, tc::mbar_wait(&bar_pv[x], (n_tiles - 1) & 1, kWaitLimit)))
+      // the last PV_x: the only commit of bar_pv with P in TMEM
+      const uint32_t pv_phase = kPTmem ? 0u : static_cast<uint32_t>((n_tiles - 1) & 1);
+      if (!__all_sync(kFullMask, tc::mbar_wait(&bar_pv[x], pv_phase, kWaitLimit)))
         *aborted = 1;
       tc::tc_fence_after();
+      if constexpr (kHalves == 2) {
+        // row sum of both halves. The partner read this slot's max before its
+        // last P arrival, which precedes the PV commit waited on above.
+        pair_red[(x * 2 + h) * kTileM + r] = l_sum;
+        pair_barrier(pair_id);
+        l_sum = pair_red[x * 2 * kTileM + r] + pair_red[(x * 2 + 1) * kTileM + r];
+      }
     }
     // epilogue (l_sum is in a register): warp-collective TMEM reads of O_x
-    if (!__any_sync(kFullMask, *aborted != 0)) {
+    if (t == n_tiles && !__any_sync(kFullMask, *aborted != 0)) {
       const bool store = qi < qlen;
-      T* dst = static_cast<T*>(p.out) + (qbegin + (store ? qi : 0)) * p.o_rs + head * p.o_hs;
+      T* dst = static_cast<T*>(p.out) + (qbegin + (store ? qi : 0)) * p.o_rs + head * p.o_hs +
+               h * kOCols;
       const float inv = l_sum > 0.f ? 1.f / l_sum : 0.f;
 #pragma unroll
-      for (int c = 0; c < 4; ++c) {
+      for (int c = 0; c < kOCols / 32; ++c) {
         uint32_t o[32];
         tc::tmem_ld32(o_tmem + c * 32, o);
         tc::tmem_ld_wait(o);
@@ -880,13 +1067,42 @@ __global__ void __launch_bounds__(kPairThreads, 1)
         }
       }
     }
-  } else if (seq >= 0 && n_tiles == 0 && warp < 8) {
+  };
+  auto zero_rows = [&]() {
     // rows that see no keys: zeros
     const int qi = m0 + (warp >> 2) * kTileM + (tid & (kTileM - 1));
     if (qi < qlen) {
       T* dst = static_cast<T*>(p.out) + (qbegin + qi) * p.o_rs + head * p.o_hs;
       for (int c = 0; c < kHeadDim; c += 8) *reinterpret_cast<uint4*>(dst + c) = make_uint4(0, 0, 0, 0);
     }
+  };
+  if constexpr (kWide) {
+    // Register reallocation per warpgroup, each from one instruction inside
+    // its warpgroup's branch so that the role code below it is compiled to
+    // the new limit: warpgroups 0-1 (softmax) rise, warpgroup 2 (MMA,
+    // producer, two idle warps) drops.
+    if (warp >= 8) {
+      tc::setmaxnreg_dec<kWideOtherRegs>();
+      if (active && warp == kProducerWarp)
+        producer_role();
+      else if (active && warp == kMmaWarp)
+        mma_role();
+    } else {
+      tc::setmaxnreg_inc<kWideSoftRegs>();
+      if (active)
+        softmax_role();
+      else if (seq >= 0 && n_tiles == 0)
+        zero_rows();
+    }
+  } else {
+    if (active && warp == kProducerWarp)
+      producer_role();
+    else if (active && warp == kMmaWarp)
+      mma_role();
+    else if (active && warp < kSoftWarps)
+      softmax_role();
+    else if (seq >= 0 && n_tiles == 0 && warp < 8)
+      zero_rows();
   }
   __syncthreads();
   if (*aborted && tid == 0) raise_status(p.status, kStatusTimeout);
@@ -927,22 +1143,33 @@ bool encode(CUtensorMap* map, CUtensorMapDataType type, uint32_t rank, const voi
 
 bool aligned16(const void* ptr) { return (reinterpret_cast<uintptr_t>(ptr) & 15u) == 0; }
 
-// Which tensor-core kernel rlt_paged_prefill launches: 3 = warp-specialised
-// two-tile kernel with P in TMEM (default), 2 = the same with P in shared
-// memory, 1 = the single-tile kernel.
-std::atomic<int> g_prefill_version{3};
+// Which tensor-core kernel rlt_paged_prefill launches: 5 = warp-specialised
+// two-tile kernel with P in TMEM and register-resident scores (default), 4 =
+// split softmax (two warps per row set), 3 = one warp per row set reading S
+// from TMEM twice, 2 = as 3 with P in shared memory, 1 = the single-tile
+// kernel.
+std::atomic<int> g_prefill_version{5};
 
-template <typename T, bool kPTmem>
+template <typename T, bool kPTmem, int kHalves, bool kWide = false>
 cudaError_t launch_pair(dim3 grid, const PrefillTcParams& p, cudaStream_t stream) {
   constexpr int bytes = PairLayout<kPTmem>::kSmemBytes;
   static std::once_flag once;
   static cudaError_t attr_err = cudaSuccess;
   std::call_once(once, [] {
-    attr_err = cudaFuncSetAttribute(paged_prefill_tc2_kernel<T, kPTmem>,
+    attr_err = cudaFuncSetAttribute(paged_prefill_tc2_kernel<T, kPTmem, kHalves, kWide>,
                                     cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+    if (kWide && attr_err == cudaSuccess) {
+      // the register split assumes this launch allocation; with fewer
+      // registers the softmax warpgroups' increase could never be granted
+      cudaFuncAttributes attr{};
+      attr_err = cudaFuncGetAttributes(&attr, paged_prefill_tc2_kernel<T, kPTmem, kHalves, kWide>);
+      if (attr_err == cudaSuccess && attr.numRegs < kWideLaunchRegs)
+        attr_err = cudaErrorInvalidConfiguration;
+    }
   });
   if (attr_err != cudaSuccess) return attr_err;
-  paged_prefill_tc2_kernel<T, kPTmem><<<grid, kPairThreads, bytes, stream>>>(p);
+  paged_prefill_tc2_kernel<T, kPTmem, kHalves, kWide>
+      <<<grid, pair_threads(kHalves, kWide), bytes, stream>>>(p);
   return cudaSuccess;
 }
 
@@ -1036,11 +1263,17 @@ int paged_prefill_tc(const void* q, const void* key_cache, const void* value_cac
   const dim3 grid(static_cast<unsigned>((num_tokens + kPairRows - 1) / kPairRows + num_seqs), hq);
   cudaError_t err;
   if (version == 2)
-    err = dtype == RLT_BF16 ? launch_pair<__nv_bfloat16, false>(grid, p, stream)
-                            : launch_pair<__half, false>(grid, p, stream);
+    err = dtype == RLT_BF16 ? launch_pair<__nv_bfloat16, false, 1>(grid, p, stream)
+                            : launch_pair<__half, false, 1>(grid, p, stream);
+  else if (version == 3)
+    err = dtype == RLT_BF16 ? launch_pair<__nv_bfloat16, true, 1>(grid, p, stream)
+                            : launch_pair<__half, true, 1>(grid, p, stream);
+  else if (version == 4)
+    err = dtype == RLT_BF16 ? launch_pair<__nv_bfloat16, true, 2>(grid, p, stream)
+                            : launch_pair<__half, true, 2>(grid, p, stream);
   else
-    err = dtype == RLT_BF16 ? launch_pair<__nv_bfloat16, true>(grid, p, stream)
-                            : launch_pair<__half, true>(grid, p, stream);
+    err = dtype == RLT_BF16 ? launch_pair<__nv_bfloat16, true, 1, true>(grid, p, stream)
+                            : launch_pair<__half, true, 1, true>(grid, p, stream);
   if (err != cudaSuccess) return static_cast<int>(err);
   return launch_status(cudaGetLastError());
 }
@@ -1049,7 +1282,7 @@ int paged_prefill_tc(const void* q, const void* key_cache, const void* value_cac
 }  // namespace rlt
 
 extern "C" int rlt_prefill_tc_select(int32_t version) {
-  if (version < 1 || version > 3) return rlt::g_prefill_version.load();
+  if (version < 1 || version > 5) return rlt::g_prefill_version.load();
   return rlt::g_prefill_version.exchange(version);
 }
 

@@ -57,6 +57,41 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
   return done != 0;
 }
 
+// Register reallocation between warpgroups: every warp of a warpgroup
+// executes the same instruction; an increase waits until decreases elsewhere
+// in the CTA have released enough of the launch allocation.
+template <int kRegs>
+__device__ __forceinline__ void setmaxnreg_inc() {
+  asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;\n" ::"n"(kRegs));
+}
+template <int kRegs>
+__device__ __forceinline__ void setmaxnreg_dec() {
+  asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;\n" ::"n"(kRegs));
+}
+
+// Non-blocking test of a phase (the thread is never suspended).
+__device__ __forceinline__ bool mbar_test_wait(uint64_t* bar, uint32_t parity) {
+  uint32_t done;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(done)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return done != 0;
+}
+
+// Bounded polling wait with test_wait: for a single thread whose wake-up
+// latency matters more than the shared-memory traffic of polling.
+__device__ __forceinline__ bool mbar_poll(uint64_t* bar, uint32_t parity, long long limit) {
+  const long long start = clock64();
+  while (!mbar_test_wait(bar, parity)) {
+    if (clock64() - start > limit) return false;
+  }
+  return true;
+}
+
 // Bounded wait: false if the phase did not complete within `limit` cycles.
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, long long limit) {
   if (mbar_try_wait(bar, parity)) return true;
