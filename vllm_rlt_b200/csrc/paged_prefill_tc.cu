@@ -589,16 +589,28 @@ __global__ void __launch_bounds__(pair_threads(kHalves, kWide), 1)
 
   auto producer_role = [&]() {
     // ---------------- TMA producer. The warp's lanes fetch the block ids of
-    // a key tile together (lane j: page j) one tile ahead of its copies, so
-    // no table read sits between two copies; lane 0 issues the copies.
+    // a key tile together (lane j: page j) a tile ahead of its copies and
+    // check them only when the copies are issued, so neither the table read
+    // nor its latency sits between two copies; lane j issues page j's copies.
     const int pages_per_tile = kTileN / p.page;
+    struct PageId {
+      int raw;
+      bool live;  // a page of the context (else the copy zero-fills)
+    };
     auto tile_pages = [&](int t) {
-      int blk = static_cast<int>(p.num_blocks);  // out of range: zero fill
+      PageId id{0, false};
       const int logical = t * pages_per_tile + lane;
       if (lane < pages_per_tile && t < n_tiles && logical * p.page < ctx) {
-        const int b = p.tables[seq * p.t_rs + logical];
-        if (b >= 0 && b < p.num_blocks)
-          blk = b;
+        id.raw = p.tables[seq * p.t_rs + logical];
+        id.live = true;
+      }
+      return id;
+    };
+    auto block_of = [&](PageId id) {
+      int blk = static_cast<int>(p.num_blocks);  // out of range: zero fill
+      if (id.live) {
+        if (id.raw >= 0 && id.raw < p.num_blocks)
+          blk = id.raw;
         else
           raise_status(p.status, kStatusBadBlock);
       }
@@ -609,8 +621,8 @@ __global__ void __launch_bounds__(pair_threads(kHalves, kWide), 1)
       tc::prefetch_tensormap(&p.kmap);
       tc::prefetch_tensormap(&p.vmap);
     }
-    int cur = tile_pages(0);
-    int nxt = tile_pages(1);
+    int cur = block_of(tile_pages(0));
+    PageId nxt = tile_pages(1);
     if (lane == 0) {
       tc::mbar_expect_tx(&bar_q, 2 * kTileBytes);
       for (int x = 0; x < 2; ++x)
@@ -647,7 +659,7 @@ __global__ void __launch_bounds__(pair_threads(kHalves, kWide), 1)
       }
       ++issued;
       if (i & 1) {
-        cur = nxt;
+        cur = block_of(nxt);  // read a tile ago
         nxt = tile_pages((i >> 1) + 2);
       }
     }
