@@ -97,6 +97,40 @@ __device__ __forceinline__ uint64_t add2(uint64_t a, uint64_t b) {
   asm("add.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
   return r;
 }
+__device__ __forceinline__ uint64_t mul2(uint64_t a, uint64_t b) {
+  uint64_t r;
+  asm("mul.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+  return r;
+}
+
+// 2^x of a pair on the FMA pipe, to take part of the exponentials off the
+// MUFU unit. x = n + f with n = rint(x) (adding and removing 1.5 * 2^23
+// rounds to an integer), 2^f from a degree-3 polynomial fitted for this
+// kernel (least-squares minimax of the relative error on [-0.5, 0.5]; largest
+// relative error 7.5e-5 in fp32 Horner form, far below the bf16/fp16
+// rounding of P), 2^n written into the exponent field. Arguments are clamped
+// at -127, where that field is 0, so -inf gives 0 as ex2.approx.ftz does
+// (results under 2^-126 may stay denormal where that flushes them).
+__device__ __forceinline__ uint64_t exp2_poly2(float x0, float x1) {
+  constexpr float kRound = 12582912.f;  // 1.5 * 2^23
+  constexpr float kC0 = 0.9999281167984009f, kC1 = 0.6932609677314758f;
+  constexpr float kC2 = 0.24261054396629333f, kC3 = 0.05517132207751274f;
+  const uint64_t x = pk2(fmaxf(x0, -127.f), fmaxf(x1, -127.f));
+  const uint64_t t = add2(x, pk2(kRound, kRound));
+  const uint64_t n = add2(t, pk2(-kRound, -kRound));
+  const uint64_t f = fma2(n, pk2(-1.f, -1.f), x);
+  uint64_t q = fma2(pk2(kC3, kC3), f, pk2(kC2, kC2));
+  q = fma2(q, f, pk2(kC1, kC1));
+  q = fma2(q, f, pk2(kC0, kC0));
+  float t0, t1;
+  upk2(t, t0, t1);
+  // the low bits of t hold 0x400000 + n: shifted into the exponent field
+  // they give n (mod 2^32), to which the bias is added
+  const uint32_t e0 = (static_cast<uint32_t>(__float_as_int(t0)) << 23) + 0x3F800000u;
+  const uint32_t e1 = (static_cast<uint32_t>(__float_as_int(t1)) << 23) + 0x3F800000u;
+  return mul2(q, pk2(__uint_as_float(e0), __uint_as_float(e1)));
+}
+
 __device__ __forceinline__ float max3(float a, float b, float c) {
   float r;
   asm("max.f32 %0, %1, %2, %3;" : "=f"(r) : "f"(a), "f"(b), "f"(c));
@@ -451,6 +485,11 @@ constexpr int pair_threads(int halves, bool wide) { return wide ? 12 * 32 : (8 *
 // warpgroup drops to 96: 256 x 200 + 128 x 96 = 63,488 <= 384 x 168 = 64,512.
 // (216/64 and 208/80 fit as well but spill more in the MMA and producer code.)
 constexpr int kWideLaunchRegs = 168;
+// Of every 8 score pairs of a row, how many the wide softmax exponentiates
+// with the FMA-pipe polynomial instead of the MUFU unit. 1, 2 and 3 each
+// measured slower (4-8 %) on the prefill workload: the kernel runs at the
+// power cap, so the extra instructions cost clock rather than freeing MUFU.
+constexpr int kPolyPairs = 0;
 constexpr int kWideSoftRegs = 200;
 constexpr int kWideOtherRegs = 96;
 static_assert(256 * kWideSoftRegs + 128 * kWideOtherRegs <= 384 * kWideLaunchRegs,
@@ -889,8 +928,12 @@ __global__ void __launch_bounds__(pair_threads(kHalves, kWide), 1)
                 fma2(pk2(__uint_as_float(sr[c][j]), __uint_as_float(sr[c][j + 1])), scale2, neg2);
             float p0, p1;
             upk2(arg, p0, p1);
-            p0 = ex2(p0);
-            p1 = ex2(p1);
+            if ((j / 2) % 8 < kPolyPairs) {  // this pair on the FMA pipe
+              upk2(exp2_poly2(p0, p1), p0, p1);
+            } else {
+              p0 = ex2(p0);
+              p1 = ex2(p1);
+            }
             psum2 = add2(psum2, pk2(p0, p1));
             packed[j / 2] = pack2<T>(p0, p1);
           }
