@@ -123,3 +123,45 @@ def test_each_tensor_core_kernel_vs_oracle(dtype, page):
         assert_close(to_numpy(out), expected, dtype, **FA4_TOLERANCE[dtype])
         outs[version] = out
     assert torch.equal(outs[2], outs[3])
+
+
+@pytest.mark.parametrize("dtype,d,group", [("bf16", 128, 1), ("f16", 128, 2), ("f32", 64, 1)])
+def test_prefill_batch_invariance_bit_identical_sequences(dtype, d, group):
+    """A sequence's prefill output does not depend on which other sequences
+    share the launch (the decode counterpart is the reference's
+    tests/test_flash_attention.py:192-208): every tile's reduction order is
+    a function of its own sequence. Covers the tensor-core kernel (bf16 /
+    fp16, head_dim 128, GQA 1 and 2) and the CUDA-core path (fp32)."""
+    rng = np.random.default_rng(21)
+    page, hkv = 16, 2
+    prefix = [0, 300, 1100, 40]
+    chunk = [700, 260, 333, 17]
+    lengths = [s + c for s, c in zip(prefix, chunk)]
+    width = max(math.ceil(n / page) for n in lengths)
+    num_blocks = sum(math.ceil(n / page) for n in lengths) + 2
+    perm = rng.permutation(num_blocks)
+    tables = np.full((4, width), -1, dtype=np.int32)
+    c = 0
+    for i, n in enumerate(lengths):
+        tables[i, : math.ceil(n / page)] = perm[c : c + math.ceil(n / page)]
+        c += math.ceil(n / page)
+    g = torch.Generator(device="cuda").manual_seed(9)
+    td = TORCH[dtype]
+    key = torch.randn(num_blocks, page, hkv, d, generator=g, device="cuda").to(td)
+    value = torch.randn(num_blocks, page, hkv, d, generator=g, device="cuda").to(td)
+    q = [torch.randn(n, hkv * group, d, generator=g, device="cuda").to(td) for n in chunk]
+
+    def run(rows):
+        cu = np.concatenate([[0], np.cumsum([chunk[r] for r in rows])]).astype(np.int32)
+        out = rb.paged_prefill(torch.cat([q[r] for r in rows]), key, value,
+                               torch.from_numpy(tables[rows]).cuda(),
+                               torch.tensor([lengths[r] for r in rows], dtype=torch.int32,
+                                            device="cuda"),
+                               torch.from_numpy(cu).cuda(), max(chunk[r] for r in rows))
+        torch.cuda.synchronize()
+        return [out[cu[i] : cu[i + 1]] for i in range(len(rows))]
+
+    together = run([0, 1, 2, 3])
+    for rows in ([2, 3], [3, 0], [1], [2]):
+        for r, part in zip(rows, run(rows)):
+            assert torch.equal(part, together[r]), (rows, r)
