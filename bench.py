@@ -18,6 +18,12 @@ scaling); the step time is the max over ranks of the device-timed region.
 --impl reference times the reference algorithm's CPU path (the numpy
 restatement in oracle/, the reference being Python) on this box's host cores
 on a bounded sample of the same workload.
+
+--impl reference-triton times the reference's own GPU decode, its Triton
+kernel behind vllm_rlt.kernels.paged_attention.triton_paged_attention, from
+the unmodified reference installed under baseline/_ref, on the same GPU
+workload as our arm (rank 0 only; prints an "unavailable" line when that
+install or Triton is missing).
 """
 
 from __future__ import annotations
@@ -49,7 +55,7 @@ def parse():
     p.add_argument("--gpus", type=int, default=1)
     p.add_argument("--steps", type=int, default=20)
     p.add_argument("--warmup", type=int, default=5)
-    p.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    p.add_argument("--impl", choices=["ours", "reference", "reference-triton"], default="ours")
     p.add_argument("--rows", type=int, default=256)
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--no-extras", action="store_true",
@@ -225,6 +231,73 @@ def run_reference(args):
                          "kind": "port", "sample": sample},
         "e2e": {"value": round(value, 3), "unit": "GB/s", "h2d_bytes_per_step": 0,
                 "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+def run_reference_triton(args):
+    import torch
+
+    from vllm_rlt_b200 import workloads
+    from vllm_rlt_b200.kernels.paged_attention import decode_bytes
+
+    if int(os.environ.get("RANK", "0")) != 0:
+        return
+    sys.path.insert(0, str(ROOT / "baseline" / "_ref"))
+    try:
+        from vllm_rlt.kernels.paged_attention import triton_paged_attention
+    except Exception as exc:  # the install is optional
+        print(json.dumps({"impl": "reference-triton",
+                          "unavailable": f"reference not importable from baseline/_ref: {exc}"}))
+        return
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    device = torch.device("cuda", local)
+    torch.cuda.set_device(device)
+    plan = workloads.config2_plan(seed=0, rows=args.rows)
+    g = torch.Generator(device=device).manual_seed(1000)
+    shape = (plan.num_blocks, 1, plan.page, plan.num_kv_heads, plan.head_dim)
+    kpool = torch.empty(shape, device=device, dtype=torch.bfloat16)
+    vpool = torch.empty_like(kpool)
+    fill_random(kpool, g)
+    fill_random(vpool, g)
+    k_layer, v_layer = kpool[:, 0], vpool[:, 0]
+    tables = torch.from_numpy(plan.block_tables()).to(device)
+    lengths = torch.from_numpy(plan.context_lengths).to(device)
+    q = torch.randn((plan.num_rows, 16, 128), generator=g, device=device).to(torch.bfloat16)
+    step_bytes = decode_bytes(plan.context_lengths, 16, 16, 128, 2, plan.page)
+
+    def step():
+        return triton_paged_attention(q, k_layer, v_layer, tables, lengths)
+
+    for _ in range(max(args.warmup, 1)):
+        out = step()
+    torch.cuda.synchronize(device)
+    t0 = torch.cuda.Event(enable_timing=True)
+    t1 = torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clocks:
+        t0.record()
+        for _ in range(args.steps):
+            out = step()
+        t1.record()
+        torch.cuda.synchronize(device)
+    ms = t0.elapsed_time(t1) / args.steps
+    value = step_bytes / (ms / 1e3) / 1e9
+    peak, kind = measured_peak()
+    import vllm_rlt_b200 as rb
+
+    ours = rb.B200PagedAttention(device, torch.bfloat16, 128, plan.page)(q, k_layer, v_layer,
+                                                                          tables, lengths)
+    line = {
+        "metric": METRIC, "value": round(value, 2), "unit": "GB/s", "impl": "reference-triton",
+        "n_gpus": 1, "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 4),
+        "higher_is_better": True, "dtype": "bf16", "data": "synthetic",
+        "config": {"workload": WORKLOAD, "rows": plan.num_rows,
+                   "kernel": "reference _paged_attention_kernel (Triton), one program per "
+                             "(row, query head), 32-token tiles, no split-KV"},
+        "roofline": {"bound": "hbm", "achieved": round(value, 1), "peak": peak, "unit": "GB/s",
+                     "frac": round(value / peak, 4), "peak_kind": kind},
+        "max_abs_vs_ours": float((out.float() - ours.float()).abs().max()),
+        "clocks": clocks.summary(),
     }
     print(json.dumps(line), flush=True)
 
@@ -773,6 +846,8 @@ def main():
     args = parse()
     if args.impl == "reference":
         run_reference(args)
+    elif args.impl == "reference-triton":
+        run_reference_triton(args)
     else:
         run_ours(args)
 
