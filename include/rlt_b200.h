@@ -304,13 +304,26 @@ int rlt_rms_norm(const void* x, const void* weight, const void* residual, void* 
                  int32_t dtype, int32_t rows, int32_t hidden, float eps, int64_t x_stride,
                  int64_t residual_stride, int64_t out_stride, void* stream);
 
+/* rlt_rms_norm followed by a second RMSNorm of its output in one launch:
+ * out = [residual +] weight * norm(x); out2 = weight2 * norm(out), out2
+ * computed from out's rounded values, bit-identical to two rlt_rms_norm
+ * calls. The decoder layer's residual stream feeds one norm into the next:
+ * post-attention norm + residual -> MLP input norm, and post-MLP norm +
+ * residual -> the next layer's input norm (or the final norm). Needs 16-byte
+ * aligned rows (RLT_E_ALIGN otherwise); hidden <= 4096.
+ * Replaces: vllm_rlt/models/ouro.py:118-125 and :143-147 (two norm calls). */
+int rlt_rms_norm2(const void* x, const void* weight, const void* residual, void* out,
+                  const void* weight2, void* out2, int32_t dtype, int32_t rows, int32_t hidden,
+                  float eps, int64_t x_stride, int64_t residual_stride, int64_t out_stride,
+                  int64_t out2_stride, void* stream);
+
 /* RoPE on q and k straight out of the fused qkv projection, k written (with
  * v) into the KV page of its depth plane:
  *   angles = pos * inv_freq (fp32); cos/sin rounded to the dtype;
  *   x' = x * cos + rotate_half(x) * sin (each op rounded to the dtype);
  *   q_out[r] = q'; key_cache[blocks[r], layer, offsets[r]] = k'; value_cache[..] = v.
- * qkv rows hold [heads*D | kv_heads*D | kv_heads*D]. Bit-identical to the
- * unfused torch expression followed by rlt_kv_write.
+ * qkv rows hold [heads*D | kv_heads*D | kv_heads*D]; D <= 512. Bit-identical
+ * to the unfused torch expression followed by rlt_kv_write.
  * Replaces: vllm_rlt/models/ouro.py:61-75 and :104-110 plus the page write of
  * vllm_rlt/core/kv_cache_manager.py:531-532. */
 int rlt_rope_write_kv(const void* qkv, const int64_t* positions, const float* inv_freq,

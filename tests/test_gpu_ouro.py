@@ -146,13 +146,14 @@ def test_graph_replay_matches_eager_steps():
     assert torch.equal(eager.value_cache, graphed.value_cache)
 
 
+@pytest.mark.parametrize("d", [128, 24])  # 16-byte vector path; element path
 @pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16, torch.float32])
-def test_fused_rope_kv_write_is_bit_identical_to_torch(dtype):
+def test_fused_rope_kv_write_is_bit_identical_to_torch(dtype, d):
     from vllm_rlt_b200 import write_kv
     from vllm_rlt_b200.kernels import ouro_ops
 
     torch.manual_seed(0)
-    heads, kv_heads, d, n = 16, 4, 128, 37
+    heads, kv_heads, n = 16, 4, 37
     qkv = torch.randn(n, (heads + 2 * kv_heads) * d, device="cuda").to(dtype) * 3
     positions = torch.randint(0, 70000, (n,), device="cuda")
     inv_freq = 1.0 / (10000.0 ** (torch.arange(0, d, 2, device="cuda", dtype=torch.float32) / d))
@@ -194,6 +195,27 @@ def test_fused_norm_and_swiglu_match_torch(dtype):
     got = ouro_ops.silu_mul(gu, 5632)
     want = torch.nn.functional.silu(gu[:, :5632]) * gu[:, 5632:]
     torch.testing.assert_close(got, want, **tol)
+
+
+@pytest.mark.parametrize("residual", [True, False])
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float32])
+def test_norm_pair_is_bit_identical_to_two_norms(dtype, residual):
+    """rlt_rms_norm2 (norm [+ residual], then the next norm of that output,
+    one launch) equals two rlt_rms_norm calls bit for bit."""
+    from vllm_rlt_b200.kernels import ouro_ops
+
+    torch.manual_seed(2)
+    x = torch.randn(23, 2048, device="cuda").to(dtype) * 2
+    res = torch.randn(23, 2048, device="cuda").to(dtype) if residual else None
+    w = (1 + 0.1 * torch.randn(2048, device="cuda")).to(dtype)
+    w2 = (1 + 0.1 * torch.randn(2048, device="cuda")).to(dtype)
+    out, out2 = ouro_ops.rms_norm(x, w, 1e-6, residual=res, weight2=w2)
+    first = ouro_ops.rms_norm(x, w, 1e-6, residual=res)
+    second = ouro_ops.rms_norm(first, w2, 1e-6)
+    assert torch.equal(out, first) and torch.equal(out2, second)
+    want = (res if residual else 0) + rms_norm(x, w, 1e-6)
+    tol = dict(atol=0, rtol=2**-7) if dtype == torch.bfloat16 else dict(atol=1e-5, rtol=1e-5)
+    torch.testing.assert_close(out, want.to(dtype), **tol)
 
 
 def test_fused_decoder_matches_unfused_decoder():

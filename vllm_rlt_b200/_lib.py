@@ -86,6 +86,7 @@ SIGNATURES = {
     "rlt_stage_prefill": (_i32, [_p, _p, _p, _i64, _p]),
     "rlt_expand_prefill": (_i32, [_p] * 6 + [_i64, _i32, _i32, _i64, _p]),
     "rlt_rms_norm": (_i32, [_p] * 4 + [_i32] * 3 + [_f32] + [_i64] * 3 + [_p]),
+    "rlt_rms_norm2": (_i32, [_p] * 6 + [_i32] * 3 + [_f32] + [_i64] * 4 + [_p]),
     "rlt_rope_write_kv": (_i32, [_p] * 9 + [_i32] * 7 + [_i64] * 8 + [_p]),
     "rlt_silu_mul": (_i32, [_p, _p, _i32, _i32, _i32, _i64, _i64, _p]),
     "rlt_copy_segments": (_i32, [_p, _i32, _i64, _p, _p]),

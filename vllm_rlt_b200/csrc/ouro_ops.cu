@@ -66,6 +66,91 @@ __global__ void __launch_bounds__(256) rms_norm_kernel(const T* __restrict__ x, 
   }
 }
 
+// Sum of `v` over the CTA (blockDim a multiple of 32, at most 1024); every
+// thread gets the total. `partial` holds 33 floats; it is reused by the next
+// call only after the __syncthreads that ends this one.
+__device__ __forceinline__ float block_sum(float v, float* partial) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(kFullMask, v, o);
+  if ((threadIdx.x & 31) == 0) partial[threadIdx.x >> 5] = v;
+  __syncthreads();
+  if (threadIdx.x < 32) {
+    float t = threadIdx.x < (blockDim.x >> 5) ? partial[threadIdx.x] : 0.f;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) t += __shfl_xor_sync(kFullMask, t, o);
+    if (threadIdx.x == 0) partial[32] = t;
+  }
+  __syncthreads();
+  return partial[32];
+}
+
+// The same norm on 16-byte vectors (hidden a multiple of the vector width,
+// rows 16-byte aligned), each thread holding up to kNV consecutive vectors of
+// the row. With w2 set it also writes out2 = RMSNorm(out; w2): the residual
+// stream's next norm (ouro.py:118-125, the post-attention norm's output feeds
+// the MLP norm; a layer's output feeds the next layer's input norm or the
+// final norm), so the pair costs one launch and one read of the row.
+template <typename T, int kNV>
+__global__ void __launch_bounds__(256) rms_norm_vec_kernel(
+    const T* __restrict__ x, const T* __restrict__ w, const T* __restrict__ residual,
+    T* __restrict__ out, const T* __restrict__ w2, T* __restrict__ out2, int hidden, float eps,
+    int64_t x_stride, int64_t r_stride, int64_t o_stride, int64_t o2_stride) {
+  constexpr int V = 16 / sizeof(T);
+  __shared__ float partial[33];
+  const int row = blockIdx.x;
+  const int nvec = hidden / V;
+  float vals[kNV][V];
+  float ss = 0.f;
+#pragma unroll
+  for (int k = 0; k < kNV; ++k) {
+    const int vi = threadIdx.x + k * blockDim.x;
+    if (vi < nvec) {
+      unpack16<T>(ld_vec(x + row * x_stride + vi * V), vals[k]);
+    } else {
+#pragma unroll
+      for (int e = 0; e < V; ++e) vals[k][e] = 0.f;
+    }
+#pragma unroll
+    for (int e = 0; e < V; ++e) ss = fmaf(vals[k][e], vals[k][e], ss);
+  }
+  const float inv = rsqrtf(block_sum(ss, partial) / static_cast<float>(hidden) + eps);
+  float ss2 = 0.f;
+#pragma unroll
+  for (int k = 0; k < kNV; ++k) {
+    const int vi = threadIdx.x + k * blockDim.x;
+    if (vi >= nvec) continue;
+    float wv[V], y[V];
+    unpack16<T>(ld_vec(w + vi * V), wv);
+    if (residual != nullptr) {
+      float rv[V];
+      unpack16<T>(ld_vec(residual + row * r_stride + vi * V), rv);
+#pragma unroll
+      for (int e = 0; e < V; ++e) y[e] = rnd<T>(add(rv[e], rnd<T>(mul(wv[e], rnd<T>(mul(vals[k][e], inv))))));
+    } else {
+#pragma unroll
+      for (int e = 0; e < V; ++e) y[e] = rnd<T>(mul(wv[e], rnd<T>(mul(vals[k][e], inv))));
+    }
+    st_vec(out + row * o_stride + vi * V, pack16<T>(y));
+#pragma unroll
+    for (int e = 0; e < V; ++e) {
+      vals[k][e] = y[e];
+      ss2 = fmaf(y[e], y[e], ss2);
+    }
+  }
+  if (w2 == nullptr) return;  // uniform over the CTA
+  const float inv2 = rsqrtf(block_sum(ss2, partial) / static_cast<float>(hidden) + eps);
+#pragma unroll
+  for (int k = 0; k < kNV; ++k) {
+    const int vi = threadIdx.x + k * blockDim.x;
+    if (vi >= nvec) continue;
+    float wv[V], y[V];
+    unpack16<T>(ld_vec(w2 + vi * V), wv);
+#pragma unroll
+    for (int e = 0; e < V; ++e) y[e] = rnd<T>(mul(wv[e], rnd<T>(mul(vals[k][e], inv2))));
+    st_vec(out2 + row * o2_stride + vi * V, pack16<T>(y));
+  }
+}
+
 // vllm_rlt/models/ouro.py:61-75 and :104-110, fused with the page write of
 // vllm_rlt/core/kv_cache_manager.py:531-532:
 //   angles = pos.float() * inv_freq  (fp32), cat(angles, angles)
@@ -73,7 +158,12 @@ __global__ void __launch_bounds__(256) rms_norm_kernel(const T* __restrict__ x, 
 //   q' = q * cos + rotate_half(q) * sin  (each op rounded to dtype), same for k
 //   key_cache[block, layer, offset] = k'; value_cache[...] = v
 // grid = rows, block = (heads + kv_heads) * head_dim / 2 pairs, capped.
-template <typename T>
+// cos/sin depend only on (row, i): computed once per row into shared memory
+// (ouro.py:61-70 computes them once per position too). kVec moves q, k and v
+// as 16-byte vectors (every pointer and stride 16-byte aligned, head_dim a
+// multiple of two vectors); otherwise element by element.
+constexpr int kRopeMaxHalf = 256;  // head_dim <= 512
+template <typename T, bool kVec>
 __global__ void __launch_bounds__(256) rope_write_kernel(
     const T* __restrict__ qkv, const int64_t* __restrict__ positions,
     const float* __restrict__ inv_freq, T* __restrict__ q_out, T* __restrict__ kc,
@@ -81,9 +171,15 @@ __global__ void __launch_bounds__(256) rope_write_kernel(
     int32_t* status, int heads, int kv_heads, int head_dim, int layer, int page,
     int64_t num_blocks, int64_t qkv_stride, int64_t q_rs, int64_t q_hs, int64_t c_bs,
     int64_t c_ls, int64_t c_ts, int64_t c_hs) {
+  __shared__ float cs[2][kRopeMaxHalf];
   const int row = blockIdx.x;
   const int half = head_dim / 2;
   const float pos = static_cast<float>(positions[row]);
+  for (int i = threadIdx.x; i < half; i += blockDim.x) {
+    const float angle = mul(pos, inv_freq[i]);
+    cs[0][i] = rnd<T>(cosf(angle));
+    cs[1][i] = rnd<T>(sinf(angle));
+  }
   const T* src = qkv + row * qkv_stride;
   const int64_t blk = blocks[row];
   const int64_t off = offsets[row];
@@ -91,34 +187,68 @@ __global__ void __launch_bounds__(256) rope_write_kernel(
   if (!ok && threadIdx.x == 0)
     raise_status(status, (blk < 0 || blk >= num_blocks) ? kStatusBadBlock : kStatusBadOffset);
   const int64_t cache_row = blk * c_bs + layer * c_ls + off * c_ts;
-  const int rotated = (heads + kv_heads) * half;  // (head, i) pairs that get RoPE
-  for (int idx = threadIdx.x; idx < rotated; idx += blockDim.x) {
-    const int h = idx / half;
-    const int i = idx - h * half;
-    const float angle = mul(pos, inv_freq[i]);
-    const float c = rnd<T>(cosf(angle));
-    const float s = rnd<T>(sinf(angle));
-    const float x1 = to_f32<T>(src[h * head_dim + i]);
-    const float x2 = to_f32<T>(src[h * head_dim + i + half]);
-    // first half: x1*cos + (-x2)*sin ; second half: x2*cos + x1*sin
-    const T y1 = from_f32<T>(add(rnd<T>(mul(x1, c)), rnd<T>(mul(-x2, s))));
-    const T y2 = from_f32<T>(add(rnd<T>(mul(x2, c)), rnd<T>(mul(x1, s))));
-    if (h < heads) {
-      T* dst = q_out + row * q_rs + h * q_hs;
-      dst[i] = y1;
-      dst[i + half] = y2;
-    } else if (ok) {
-      T* dst = kc + cache_row + (h - heads) * c_hs;
-      dst[i] = y1;
-      dst[i + half] = y2;
+  __syncthreads();
+  // first half: x1*cos + (-x2)*sin ; second half: x2*cos + x1*sin
+  auto rotate = [&](float x1, float x2, int i, float& y1, float& y2) {
+    const float c = cs[0][i], sn = cs[1][i];
+    y1 = add(rnd<T>(mul(x1, c)), rnd<T>(mul(-x2, sn)));
+    y2 = add(rnd<T>(mul(x2, c)), rnd<T>(mul(x1, sn)));
+  };
+  if constexpr (kVec) {
+    constexpr int V = 16 / sizeof(T);
+    const int chunks = half / V;
+    const int tasks = (heads + kv_heads) * chunks;
+    for (int idx = threadIdx.x; idx < tasks; idx += blockDim.x) {
+      const int h = idx / chunks;
+      const int i0 = (idx - h * chunks) * V;
+      float a[V], b[V], y1[V], y2[V];
+      unpack16<T>(ld_vec(src + h * head_dim + i0), a);
+      unpack16<T>(ld_vec(src + h * head_dim + i0 + half), b);
+#pragma unroll
+      for (int e = 0; e < V; ++e) rotate(a[e], b[e], i0 + e, y1[e], y2[e]);
+      T* dst;
+      if (h < heads)
+        dst = q_out + row * q_rs + h * q_hs;
+      else if (ok)
+        dst = kc + cache_row + (h - heads) * c_hs;
+      else
+        continue;
+      st_vec(dst + i0, pack16<T>(y1));
+      st_vec(dst + i0 + half, pack16<T>(y2));
     }
-  }
-  if (!ok) return;
-  const T* vsrc = src + (heads + kv_heads) * head_dim;
-  for (int idx = threadIdx.x; idx < kv_heads * head_dim; idx += blockDim.x) {
-    const int h = idx / head_dim;
-    const int d = idx - h * head_dim;
-    vc[cache_row + h * c_hs + d] = vsrc[idx];
+    if (!ok) return;
+    const T* vsrc = src + (heads + kv_heads) * head_dim;
+    const int vper = head_dim / V;
+    for (int idx = threadIdx.x; idx < kv_heads * vper; idx += blockDim.x) {
+      const int h = idx / vper;
+      const int d = (idx - h * vper) * V;
+      st_vec(vc + cache_row + h * c_hs + d, ld_vec(vsrc + h * head_dim + d));
+    }
+  } else {
+    const int rotated = (heads + kv_heads) * half;  // (head, i) pairs that get RoPE
+    for (int idx = threadIdx.x; idx < rotated; idx += blockDim.x) {
+      const int h = idx / half;
+      const int i = idx - h * half;
+      float y1, y2;
+      rotate(to_f32<T>(src[h * head_dim + i]), to_f32<T>(src[h * head_dim + i + half]), i, y1,
+             y2);
+      if (h < heads) {
+        T* dst = q_out + row * q_rs + h * q_hs;
+        dst[i] = from_f32<T>(y1);
+        dst[i + half] = from_f32<T>(y2);
+      } else if (ok) {
+        T* dst = kc + cache_row + (h - heads) * c_hs;
+        dst[i] = from_f32<T>(y1);
+        dst[i + half] = from_f32<T>(y2);
+      }
+    }
+    if (!ok) return;
+    const T* vsrc = src + (heads + kv_heads) * head_dim;
+    for (int idx = threadIdx.x; idx < kv_heads * head_dim; idx += blockDim.x) {
+      const int h = idx / head_dim;
+      const int d = idx - h * head_dim;
+      vc[cache_row + h * c_hs + d] = vsrc[idx];
+    }
   }
 }
 
@@ -139,6 +269,76 @@ __global__ void silu_mul_kernel(const T* __restrict__ gu, T* __restrict__ out, i
 
 int esize(int32_t dtype) { return dtype == RLT_F32 ? 4 : (dtype == RLT_F16 || dtype == RLT_BF16) ? 2 : 0; }
 
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+bool stride16(int64_t stride, int es) { return (stride * es) % 16 == 0; }
+
+template <typename T>
+int launch_rms_norm(const void* x, const void* weight, const void* residual, void* out,
+                    const void* weight2, void* out2, int rows, int hidden, float eps,
+                    int64_t x_stride, int64_t r_stride, int64_t o_stride, int64_t o2_stride,
+                    cudaStream_t s) {
+  constexpr int V = 16 / sizeof(T);
+  const int es = sizeof(T);
+  const bool vec = hidden % V == 0 && aligned16(x) && aligned16(weight) && aligned16(out) &&
+                   (residual == nullptr || (aligned16(residual) && stride16(r_stride, es))) &&
+                   (weight2 == nullptr || (aligned16(weight2) && aligned16(out2) &&
+                                           stride16(o2_stride, es))) &&
+                   stride16(x_stride, es) && stride16(o_stride, es);
+  const T* xp = static_cast<const T*>(x);
+  const T* wp = static_cast<const T*>(weight);
+  const T* rp = static_cast<const T*>(residual);
+  T* op = static_cast<T*>(out);
+  if (vec) {
+    const int nvec = hidden / V;
+    const int threads = nvec >= 256 ? 256 : (nvec + 31) / 32 * 32;
+    const int per = (nvec + threads - 1) / threads;
+    const T* w2p = static_cast<const T*>(weight2);
+    T* o2p = static_cast<T*>(out2);
+#define RLT_NORM_VEC(NV)                                                                    \
+  rms_norm_vec_kernel<T, NV><<<rows, threads, 0, s>>>(xp, wp, rp, op, w2p, o2p, hidden, eps, \
+                                                      x_stride, r_stride, o_stride, o2_stride)
+    if (per == 1)
+      RLT_NORM_VEC(1);
+    else if (per == 2)
+      RLT_NORM_VEC(2);
+    else if (per <= 4)
+      RLT_NORM_VEC(4);
+    else
+      return RLT_E_SHAPE;
+#undef RLT_NORM_VEC
+    return launch_status(cudaGetLastError());
+  }
+  if (weight2 != nullptr) return RLT_E_ALIGN;  // the fused pair needs the vector layout
+  const int threads = hidden >= 2048 ? 256 : 128;
+  if (hidden > threads * 16) return RLT_E_SHAPE;
+  rms_norm_kernel<T><<<rows, threads, 0, s>>>(xp, wp, rp, op, hidden, eps, x_stride, r_stride,
+                                              o_stride);
+  return launch_status(cudaGetLastError());
+}
+
+int rms_norm_entry(const void* x, const void* weight, const void* residual, void* out,
+                   const void* weight2, void* out2, int32_t dtype, int32_t rows, int32_t hidden,
+                   float eps, int64_t x_stride, int64_t residual_stride, int64_t out_stride,
+                   int64_t out2_stride, void* stream) {
+  if (esize(dtype) == 0) return RLT_E_DTYPE;
+  if (rows < 0 || hidden <= 0 || hidden > 16 * 256) return RLT_E_SHAPE;
+  if ((weight2 == nullptr) != (out2 == nullptr)) return RLT_E_SHAPE;
+  if (rows == 0) return RLT_OK;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  switch (dtype) {
+    case RLT_F32:
+      return launch_rms_norm<float>(x, weight, residual, out, weight2, out2, rows, hidden, eps,
+                                    x_stride, residual_stride, out_stride, out2_stride, s);
+    case RLT_F16:
+      return launch_rms_norm<__half>(x, weight, residual, out, weight2, out2, rows, hidden, eps,
+                                     x_stride, residual_stride, out_stride, out2_stride, s);
+    default:
+      return launch_rms_norm<__nv_bfloat16>(x, weight, residual, out, weight2, out2, rows,
+                                            hidden, eps, x_stride, residual_stride, out_stride,
+                                            out2_stride, s);
+  }
+}
+
 }  // namespace
 }  // namespace rlt
 
@@ -148,18 +348,16 @@ extern "C" int rlt_rms_norm(const void* x, const void* weight, const void* resid
                             int32_t dtype, int32_t rows, int32_t hidden, float eps,
                             int64_t x_stride, int64_t residual_stride, int64_t out_stride,
                             void* stream) {
-  if (esize(dtype) == 0) return RLT_E_DTYPE;
-  if (rows < 0 || hidden <= 0 || hidden > 16 * 256) return RLT_E_SHAPE;
-  if (rows == 0) return RLT_OK;
-  cudaStream_t s = static_cast<cudaStream_t>(stream);
-  const int threads = hidden >= 2048 ? 256 : 128;
-  if (hidden > threads * 16) return RLT_E_SHAPE;
-  switch (dtype) {
-    case RLT_F32: rms_norm_kernel<float><<<rows, threads, 0, s>>>(static_cast<const float*>(x), static_cast<const float*>(weight), static_cast<const float*>(residual), static_cast<float*>(out), hidden, eps, x_stride, residual_stride, out_stride); break;
-    case RLT_F16: rms_norm_kernel<__half><<<rows, threads, 0, s>>>(static_cast<const __half*>(x), static_cast<const __half*>(weight), static_cast<const __half*>(residual), static_cast<__half*>(out), hidden, eps, x_stride, residual_stride, out_stride); break;
-    default: rms_norm_kernel<__nv_bfloat16><<<rows, threads, 0, s>>>(static_cast<const __nv_bfloat16*>(x), static_cast<const __nv_bfloat16*>(weight), static_cast<const __nv_bfloat16*>(residual), static_cast<__nv_bfloat16*>(out), hidden, eps, x_stride, residual_stride, out_stride); break;
-  }
-  return launch_status(cudaGetLastError());
+  return rms_norm_entry(x, weight, residual, out, nullptr, nullptr, dtype, rows, hidden, eps,
+                        x_stride, residual_stride, out_stride, 0, stream);
+}
+
+extern "C" int rlt_rms_norm2(const void* x, const void* weight, const void* residual, void* out,
+                             const void* weight2, void* out2, int32_t dtype, int32_t rows,
+                             int32_t hidden, float eps, int64_t x_stride, int64_t residual_stride,
+                             int64_t out_stride, int64_t out2_stride, void* stream) {
+  return rms_norm_entry(x, weight, residual, out, weight2, out2, dtype, rows, hidden, eps,
+                        x_stride, residual_stride, out_stride, out2_stride, stream);
 }
 
 extern "C" int rlt_rope_write_kv(const void* qkv, const int64_t* positions, const float* inv_freq,
@@ -173,13 +371,24 @@ extern "C" int rlt_rope_write_kv(const void* qkv, const int64_t* positions, cons
                                  int64_t cache_token_stride, int64_t cache_head_stride,
                                  void* stream) {
   if (esize(dtype) == 0) return RLT_E_DTYPE;
-  if (head_dim <= 0 || head_dim % 2) return RLT_E_HEAD_DIM;
+  if (head_dim <= 0 || head_dim % 2 || head_dim / 2 > kRopeMaxHalf) return RLT_E_HEAD_DIM;
   if (heads <= 0 || kv_heads <= 0 || heads % kv_heads) return RLT_E_HEADS;
   if (rows < 0 || layer < 0 || page_size <= 0 || num_blocks < 0) return RLT_E_SHAPE;
   if (rows == 0) return RLT_OK;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const int es = esize(dtype);
+  const bool vec = head_dim % (2 * (16 / es)) == 0 && aligned16(qkv) && aligned16(q_out) &&
+                   aligned16(key_cache) && aligned16(value_cache) && stride16(qkv_stride, es) &&
+                   stride16(q_row_stride, es) && stride16(q_head_stride, es) &&
+                   stride16(cache_block_stride, es) && stride16(cache_layer_stride, es) &&
+                   stride16(cache_token_stride, es) && stride16(cache_head_stride, es);
 #define RLT_ROPE_LAUNCH(T)                                                                      \
-  rope_write_kernel<T><<<rows, 256, 0, s>>>(                                                    \
+  if (vec)                                                                                      \
+    RLT_ROPE_KERNEL(T, true);                                                                   \
+  else                                                                                          \
+    RLT_ROPE_KERNEL(T, false)
+#define RLT_ROPE_KERNEL(T, VEC)                                                                 \
+  rope_write_kernel<T, VEC><<<rows, 256, 0, s>>>(                                               \
       static_cast<const T*>(qkv), positions, inv_freq, static_cast<T*>(q_out),                  \
       static_cast<T*>(key_cache), static_cast<T*>(value_cache), write_blocks, write_offsets,    \
       status, heads, kv_heads, head_dim, layer, page_size, num_blocks, qkv_stride, q_row_stride, \
@@ -191,6 +400,7 @@ extern "C" int rlt_rope_write_kv(const void* qkv, const int64_t* positions, cons
     default: RLT_ROPE_LAUNCH(__nv_bfloat16); break;
   }
 #undef RLT_ROPE_LAUNCH
+#undef RLT_ROPE_KERNEL
   return launch_status(cudaGetLastError());
 }
 

@@ -9,18 +9,32 @@ import torch
 from .. import _lib
 
 
-def rms_norm(x, weight, eps, residual=None, out=None):
-    """weight * to_dtype(x * rsqrt(mean(x^2) + eps)) [+ residual]."""
+def rms_norm(x, weight, eps, residual=None, out=None, weight2=None, out2=None):
+    """weight * to_dtype(x * rsqrt(mean(x^2) + eps)) [+ residual].
+
+    With ``weight2`` the same launch also returns the next norm of that
+    result, ``(out, rms_norm(out, weight2, eps))``, bit-identical to two calls."""
     if x.stride(-1) != 1:
         x = x.contiguous()
     out = torch.empty_like(x) if out is None else out
     rows, hidden = x.shape
-    code = _lib.load().rlt_rms_norm(
-        x.data_ptr(), weight.data_ptr(), _lib.ptr(residual), out.data_ptr(),
-        _lib.DTYPE_CODES[x.dtype], rows, hidden, float(eps), x.stride(0),
-        0 if residual is None else residual.stride(0), out.stride(0), _lib.stream_of(x.device))
-    _lib.check(code, "rms norm")
-    return out
+    lib = _lib.load()
+    if weight2 is None:
+        code = lib.rlt_rms_norm(
+            x.data_ptr(), weight.data_ptr(), _lib.ptr(residual), out.data_ptr(),
+            _lib.DTYPE_CODES[x.dtype], rows, hidden, float(eps), x.stride(0),
+            0 if residual is None else residual.stride(0), out.stride(0),
+            _lib.stream_of(x.device))
+        _lib.check(code, "rms norm")
+        return out
+    out2 = torch.empty_like(x) if out2 is None else out2
+    code = lib.rlt_rms_norm2(
+        x.data_ptr(), weight.data_ptr(), _lib.ptr(residual), out.data_ptr(), weight2.data_ptr(),
+        out2.data_ptr(), _lib.DTYPE_CODES[x.dtype], rows, hidden, float(eps), x.stride(0),
+        0 if residual is None else residual.stride(0), out.stride(0), out2.stride(0),
+        _lib.stream_of(x.device))
+    _lib.check(code, "rms norm pair")
+    return out, out2
 
 
 def rope_write_kv(qkv, positions, inv_freq, key_cache, value_cache, layer, write_blocks,

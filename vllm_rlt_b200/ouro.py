@@ -160,8 +160,6 @@ class OuroDecoder:
         return angles.cos().to(self.dtype).unsqueeze(1), angles.sin().to(self.dtype).unsqueeze(1)
 
     def layer(self, index, hidden, cos, sin):
-        if self.fused:
-            return self.layer_fused(index, hidden)
         s, w = self.shape, self.w
         norms = w.norms[index]
         x = rms_norm(hidden, norms[0], s.eps)
@@ -184,13 +182,15 @@ class OuroDecoder:
         mlp = (torch.nn.functional.silu(gate) * up) @ w.wdown[index].t()
         return hidden + rms_norm(mlp, norms[3], s.eps)
 
-    def layer_fused(self, index, hidden):
-        """The same layer with the glue on fused kernels: one RMSNorm kernel per
-        norm (the residual add folded into the norm that precedes it), RoPE
-        fused with the page write, one SwiGLU kernel."""
+    def layer_fused(self, index, hidden, x, next_norm):
+        """The same layer with the glue on fused kernels: the residual add folded
+        into the norm before it, and each norm of the residual stream paired in
+        one launch with the norm that reads its output (post-attention -> MLP
+        input; post-MLP -> ``next_norm``, the next layer's input norm or the
+        final norm); RoPE fused with the page write; one SwiGLU kernel. ``x`` is
+        this layer's normed input; returns (hidden, next_norm(hidden))."""
         s, w = self.shape, self.w
         norms = w.norms[index]
-        x = ouro_ops.rms_norm(hidden, norms[0], s.eps)
         qkv = x @ w.wqkv[index].t()
         q = ouro_ops.rope_write_kv(qkv, self.positions, w.inv_freq, self.key_cache,
                                    self.value_cache, index, self.write_blocks,
@@ -198,20 +198,24 @@ class OuroDecoder:
         attn = self.attention(q, self.key_cache[:, index], self.value_cache[:, index],
                               self.row_tables, self.lengths)
         out = attn.reshape(hidden.shape[0], -1) @ w.wo[index].t()
-        hidden = ouro_ops.rms_norm(out, norms[1], s.eps, residual=hidden)
-        gu = ouro_ops.rms_norm(hidden, norms[2], s.eps) @ w.wgu[index].t()
-        mlp = ouro_ops.silu_mul(gu, s.intermediate) @ w.wdown[index].t()
-        return ouro_ops.rms_norm(mlp, norms[3], s.eps, residual=hidden)
+        hidden, x2 = ouro_ops.rms_norm(out, norms[1], s.eps, residual=hidden, weight2=norms[2])
+        mlp = ouro_ops.silu_mul(x2 @ w.wgu[index].t(), s.intermediate) @ w.wdown[index].t()
+        return ouro_ops.rms_norm(mlp, norms[3], s.eps, residual=hidden, weight2=next_norm)
 
     def core(self, hidden):
         """One recurrent pass: all layers, final norm, exit gate
         (vllm_rlt/models/ouro.py:209-217)."""
-        cos, sin = (None, None) if self.fused else self.rope(self.positions)
-        for index in range(self.shape.layers):
-            hidden = self.layer(index, hidden, cos, sin)
+        layers = self.shape.layers
         if self.fused:
-            hidden = ouro_ops.rms_norm(hidden, self.w.final_norm, self.shape.eps)
+            x = ouro_ops.rms_norm(hidden, self.w.norms[0][0], self.shape.eps)
+            for index in range(layers):
+                nxt = self.w.norms[index + 1][0] if index + 1 < layers else self.w.final_norm
+                hidden, x = self.layer_fused(index, hidden, x, nxt)
+            hidden = x  # the final norm of the last layer's output
         else:
+            cos, sin = self.rope(self.positions)
+            for index in range(layers):
+                hidden = self.layer(index, hidden, cos, sin)
             hidden = rms_norm(hidden, self.w.final_norm, self.shape.eps)
         gate = torch.sigmoid(hidden @ self.w.gate_w.t() + self.w.gate_b).squeeze(-1)
         return hidden, gate
