@@ -823,14 +823,16 @@ def run_ours(args):
             "traffic": None if traffic is None else traffic.get("bytes_per_launch"),
         },
         "e2e": {
-            "value": round(e2e_value, 2),
+            "value": round(serial_value, 2),
             "unit": "GB/s",
             "h2d_bytes_per_step": int(h2d),
             "d2h_bytes_per_step": int(d2h),
-            "copies": "each step's inputs H2D and result D2H inside the timed region, on one "
-                      "copy stream per direction with double-buffered inputs, overlapping the "
-                      "neighbouring steps' kernels",
-            "serial_value": round(serial_value, 2),
+            "copies": "each step's inputs H2D from pinned memory, the call, its result D2H, "
+                      "in series on one stream, inside the timed region",
+            "overlapped_value": round(e2e_value, 2),
+            "overlapped": "the same steps with the copies on one stream per direction "
+                          "overlapping the neighbouring steps' kernels; varies between runs "
+                          "(host enqueue across three streams)",
         },
         "gpu_launches": launches_per_step * args.steps,
         "clocks": clocks.summary(),
