@@ -69,7 +69,7 @@ def test_backpressure_and_geometry_checks():
     assert not transport.submit("big", 0, "decode", tables, tables, 0, 64)
     assert not transport.pending
     other_k = torch.zeros(40, 2, 16, 2, 64, dtype=torch.bfloat16, device="cuda:0")
-    with pytest.raises(ValueError, match="geometry mismatch"):
+    with pytest.raises(ValueError, match="different KV geometry"):
         transport.connect("bad", other_k, torch.zeros_like(other_k))
 
 
