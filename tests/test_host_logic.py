@@ -5,6 +5,8 @@ flash_attention.py:55-57), the backend surface, and the workload plans."""
 from __future__ import annotations
 
 import math
+import sys
+from pathlib import Path
 from types import SimpleNamespace
 
 import numpy as np
@@ -39,19 +41,155 @@ def test_backend_rejects_other_architectures(monkeypatch):
         rb.B200PagedAttention(torch.device("cuda"), torch.int8, 128, 16)
 
 
-def test_backend_surface_and_install(monkeypatch):
+def test_backend_surface(monkeypatch):
     monkeypatch.setattr(torch.version, "hip", None)
     monkeypatch.setattr(torch.cuda, "get_device_capability", lambda device=None: (10, 0))
     attention = rb.B200PagedAttention(torch.device("cuda"), torch.bfloat16, 128, 16)
     assert attention.generation == 4  # receives packed prefill from the unchanged caller
     assert attention.info["backend"] == "b200" and attention.info["arch"] == "sm_100a"
-    cache = SimpleNamespace(device=torch.device("cuda"), dtype=torch.bfloat16, head_dim=128,
-                            block_size=16, attention=None, attention_info=None,
-                            _write_prepared=None)
-    proxy = type("Proxy", (), {"_write_prepared": None})
-    got = backend_mod.install(cache, graph_proxy_class=proxy)
-    assert cache.attention is got and cache.attention_info == got.info
-    assert callable(cache._write_prepared) and callable(proxy._write_prepared)
+
+
+REF = Path(__file__).resolve().parents[1] / "baseline" / "_ref"
+
+
+def _reference_cache_manager():
+    if not (REF / "vllm_rlt" / "__init__.py").exists():
+        pytest.skip("the unmodified reference is not installed under baseline/_ref")
+    if str(REF) not in sys.path:
+        sys.path.insert(0, str(REF))
+    from vllm_rlt.core.kv_cache_manager import KVCacheManager
+    from vllm_rlt.worker import cuda_graph
+
+    return KVCacheManager, cuda_graph
+
+
+def test_install_runs_the_reference_write_body_with_a_routed_page_write(monkeypatch):
+    """install() keeps the reference's own _write_prepared (validation, order of
+    checks, written-prefix bookkeeping) and replaces only its K/V index-puts by
+    one page-write call with the same addresses; here the call is recorded and
+    applied on the CPU so it can be compared with the reference's own write."""
+    KVCacheManager, cuda_graph = _reference_cache_manager()
+    monkeypatch.setattr(torch.version, "hip", None)
+    monkeypatch.setattr(torch.cuda, "get_device_capability", lambda device=None: (10, 0))
+    calls = []
+
+    def recording_write(kc, vc, layer, blocks, offsets, k, v):
+        calls.append((layer, blocks.tolist(), offsets.tolist()))
+        kc[blocks, layer, offsets] = k[: len(blocks)]
+        vc[blocks, layer, offsets] = v[: len(blocks)]
+
+    monkeypatch.setattr(backend_mod, "write_kv", recording_write)
+
+    def make():
+        torch.manual_seed(3)
+        cache = KVCacheManager(num_layers=2, num_kv_heads=1, head_dim=4, num_blocks=32,
+                               block_size=2, max_loops=4)
+        cache.key_cache.zero_()
+        cache.value_cache.zero_()
+        cache.allocate("a", 5)
+        cache.allocate("b", 3)
+        return cache
+
+    plain, routed = make(), make()
+    # The attention object needs CUDA, so point install at a CPU pool by
+    # swapping the device only for the backend's constructor.
+    monkeypatch.setattr(backend_mod, "B200PagedAttention",
+                        lambda *a, **k: SimpleNamespace(info={"backend": "b200"}))
+    backend_mod.install(routed, graph_proxy_class=None)
+    ids, depths, positions = ["a"] * 3 + ["b"] * 2, [0, 0, 0, 2, 2], [0, 1, 2, 0, 1]
+    k = torch.randn(5, 1, 4)
+    v = torch.randn(5, 1, 4)
+    for cache in (plain, routed):
+        batch = cache._prepare_batch(ids, depths, positions)
+        cache._write_prepared(1, batch, k, v)
+        read_only = cache._prepare_batch(ids[:1], depths[:1], positions[:1], for_write=False)
+        with pytest.raises(ValueError, match="read-only"):
+            cache._write_prepared(1, read_only, k[:1], v[:1])
+        with pytest.raises(ValueError, match="layer"):
+            cache._write_prepared(2, batch, k, v)
+        with pytest.raises(ValueError, match="KV heads"):
+            cache._write_prepared(1, batch, torch.randn(5, 2, 4), v)
+    assert len(calls) == 1 and calls[0][0] == 1
+    assert torch.equal(plain.key_cache, routed.key_cache)
+    assert torch.equal(plain.value_cache, routed.value_cache)
+    for name in ("a", "b"):
+        want = [[w.prefix for w in plane] for plane in plain._allocations[name].written]
+        got = [[w.prefix for w in plane] for plane in routed._allocations[name].written]
+        assert want == got
+
+
+def test_install_routes_the_graph_proxy_write_once(monkeypatch):
+    KVCacheManager, cuda_graph = _reference_cache_manager()
+    calls = []
+    monkeypatch.setattr(backend_mod, "write_kv", lambda *args: calls.append(args[2]))
+    monkeypatch.setattr(backend_mod, "B200PagedAttention",
+                        lambda *a, **k: SimpleNamespace(info={"backend": "b200"}))
+    original = cuda_graph._DeviceCache._write_prepared
+    cache = KVCacheManager(num_layers=2, num_kv_heads=1, head_dim=4, num_blocks=16,
+                           block_size=2, max_loops=4)
+    try:
+        backend_mod.install(cache, graph_proxy_class=cuda_graph._DeviceCache)
+        backend_mod.install(cache, graph_proxy_class=cuda_graph._DeviceCache)
+        assert cuda_graph._DeviceCache._rlt_original_write is original
+        cache.allocate("a", 2)
+        batch = cache._prepare_batch(["a"], [0], [1])
+        proxy = cuda_graph._DeviceCache(cache)
+        proxy._write_prepared(1, batch, torch.ones(1, 1, 4), torch.ones(1, 1, 4))
+        assert calls == [1]
+    finally:
+        backend_mod.uninstall_graph_proxy(cuda_graph._DeviceCache)
+    assert cuda_graph._DeviceCache._write_prepared is original
+
+
+def test_routing_adapters_keep_the_triton_argument_order(monkeypatch):
+    """The launch adapters accept ``kernel[grid](...)`` with the reference's
+    argument lists (vllm_rlt/worker/async_state.py:59-75, :99-111,
+    vllm_rlt/worker/model_runner.py:543-557, vllm_rlt/worker/prefill_metadata.py:
+    53-86) and forward the right values."""
+    seen = {}
+    monkeypatch.setattr(backend_mod.routing, "metadata",
+                        lambda *a: seen.__setitem__("metadata", a[8:]))
+    monkeypatch.setattr(backend_mod.routing, "gather",
+                        lambda *a: seen.__setitem__("gather", a[3:]))
+    monkeypatch.setattr(backend_mod.routing, "scatter",
+                        lambda *a: seen.__setitem__("scatter", a[3:]))
+    monkeypatch.setattr(backend_mod.cache_ops, "finalize",
+                        lambda *a, rows: seen.__setitem__("finalize", rows))
+    monkeypatch.setattr(backend_mod.prefill_metadata, "stage_prefill",
+                        lambda *a: seen.__setitem__("stage", a[3:]))
+    monkeypatch.setattr(backend_mod.prefill_metadata, "expand_prefill",
+                        lambda *a: seen.__setitem__("expand", a[5:]))
+    launches = {**backend_mod.ROUTING_LAUNCHES, **backend_mod.PREFILL_LAUNCHES}
+    t = torch.zeros
+    tables = t((3, 4, 8), dtype=torch.int32)
+    launches["metadata_kernel"][(6,)](t(6, 3), tables, *[t(6)] * 5, t(6, 8), 5, 6, 8, 16, 4, 3,
+                                      256)
+    assert seen["metadata"] == (5, 6, 16, 4, 3)
+    pool, out = t(3, 10), t(6, 10)
+    launches["gather_kernel"][(6, 1)](pool, t(6), out, 4, 10, 10, 10, 256)
+    assert seen["gather"] == (4, 6)
+    launches["scatter_kernel"][(4, 1)](out, t(6), pool, 10, 10, 10, 256)
+    assert seen["scatter"] == (4,)
+    kc = t(5, 2, 16, 2, 8)
+    launches["finalize_kernel"][(3, 4, 1)](t(3, 3), tables, kc, kc, 8, 4, 16, 2, 16,
+                                           *kc.stride()[:3], 256)
+    assert seen["finalize"] == 3
+    launches["stage_prefill"][(1,)](t(9), t(9), t(9), 9, 256)
+    assert seen["stage"] == (9,)
+    launches["expand_prefill"][(1,)](t(4), t(4), t(2, 8), t(4), t(4), 4, 8, 16, 256)
+    assert seen["expand"] == (4, 8, 16)
+    with pytest.raises(ValueError, match="WIDTH"):
+        launches["metadata_kernel"][(6,)](t(6, 3), tables, *[t(6)] * 5, t(6, 8), 5, 6, 7, 16,
+                                          4, 3, 256)
+
+
+def test_install_routing_restores_module_attributes():
+    module = SimpleNamespace(**{name: object() for name in backend_mod.ROUTING_LAUNCHES})
+    originals = dict(vars(module))
+    restore = backend_mod.install_routing(module)
+    assert all(isinstance(getattr(module, n), backend_mod._GridLaunch) for n in originals)
+    restore()
+    assert dict(vars(module)) == originals
 
 
 def test_config1_plan_shape():

@@ -92,8 +92,48 @@ class OuroWeights:
         self.gate_w = normal(1, h)
         self.gate_b = torch.zeros(1, device=device, dtype=dtype)
         self.lm_head = linear(shape.vocab, h)
-        self.inv_freq = 1.0 / (shape.rope_theta ** (
+        self.inv_freq = self.frequencies(shape, device)
+
+    @staticmethod
+    def frequencies(shape: OuroShape, device):
+        """fp32 RoPE inverse frequencies (vllm_rlt/models/ouro.py:44-52)."""
+        d = shape.head_dim
+        return 1.0 / (shape.rope_theta ** (
             torch.arange(0, d, 2, dtype=torch.float32, device=device) / d))
+
+    @classmethod
+    def from_state_dict(cls, shape: OuroShape, state, device, dtype):
+        """Weights of a reference ``OuroForCausalLM`` (its ``state_dict()``
+        names, vllm_rlt/models/ouro.py:79-217), in this decoder's layout: q/k/v
+        and gate/up concatenated, every projection held as the transposed view
+        of a contiguous [in, out] tensor."""
+        self = cls.__new__(cls)
+
+        def get(name):
+            return state[name].to(device=device, dtype=dtype)
+
+        def linear(*names):
+            weight = torch.cat([get(n) for n in names], dim=0)  # [out, in]
+            return weight.t().contiguous().t()
+
+        self.embed = get("model.embed_tokens.weight").contiguous()
+        self.wqkv, self.wo, self.wgu, self.wdown, self.norms = [], [], [], [], []
+        for i in range(shape.layers):
+            p = f"model.layers.{i}."
+            self.wqkv.append(linear(p + "self_attn.q_proj.weight", p + "self_attn.k_proj.weight",
+                                    p + "self_attn.v_proj.weight"))
+            self.wo.append(linear(p + "self_attn.o_proj.weight"))
+            self.wgu.append(linear(p + "mlp.gate_proj.weight", p + "mlp.up_proj.weight"))
+            self.wdown.append(linear(p + "mlp.down_proj.weight"))
+            self.norms.append([get(p + n + ".weight").contiguous() for n in (
+                "input_layernorm", "input_layernorm_2", "post_attention_layernorm",
+                "post_attention_layernorm_2")])
+        self.final_norm = get("model.norm.weight").contiguous()
+        self.gate_w = get("model.early_exit_gate.weight").reshape(1, shape.hidden).contiguous()
+        self.gate_b = get("model.early_exit_gate.bias").reshape(1).contiguous()
+        self.lm_head = linear("lm_head.weight")
+        self.inv_freq = self.frequencies(shape, device)
+        return self
 
 
 def rms_norm(x, weight, eps):
