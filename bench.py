@@ -15,9 +15,12 @@ Multi-GPU (torchrun, one process per GPU): request-sharded replicas with no
 collective on the data path -- every rank runs its own 256-row batch (weak
 scaling); the step time is the max over ranks of the device-timed region.
 
---impl reference times the reference algorithm's CPU path (the numpy
-restatement in oracle/, the reference being Python) on this box's host cores
-on a bounded sample of the same workload.
+--impl reference times the reference's own CPU path, torch_paged_attention
+from the unmodified reference installed under baseline/_ref (the numpy
+restatement in oracle/ when that install is absent), on all of this box's
+host cores, on the whole batch when a call fits the run's time budget and a
+stated row sample otherwise; its line also carries the reference's CPU
+KVCacheManager.write / finalize_token times.
 
 --impl reference-triton times the reference's own GPU decode, its Triton
 kernel behind vllm_rlt.kernels.paged_attention.triton_paged_attention, from
@@ -147,90 +150,179 @@ class ClockSampler:
 # --------------------------------------------------------- reference (CPU)
 
 
-def host_sample(plan, rows, seed=0):
-    """Host copy of the selected rows' K/V pages (query plane), compacted."""
-    import oracle
+def reference_module(name):
+    """Import a module of the unmodified reference installed under
+    baseline/_ref; None when that install is missing."""
+    import importlib
 
-    rng = np.random.default_rng(seed)
-    inputs = []
-    for r in rows:
-        n = int(plan.context_lengths[r])
-        pages = math.ceil(n / plan.page)
-        shape = (pages, plan.page, plan.num_kv_heads, plan.head_dim)
-        k = oracle.f32_to_bf16(rng.standard_normal(shape, dtype=np.float32))
-        v = oracle.f32_to_bf16(rng.standard_normal(shape, dtype=np.float32))
-        q = oracle.f32_to_bf16(rng.standard_normal((1, plan.num_q_heads, plan.head_dim),
-                                                   dtype=np.float32))
-        inputs.append((q, k, v, np.arange(pages, dtype=np.int32)[None], np.array([n])))
-    return inputs
-
-
-def time_cpu(inputs, threads):
-    """Run the oracle over the sample rows on ``threads`` host threads."""
-    import concurrent.futures
-
-    import oracle
-
-    def one(item):
-        q, k, v, t, n = item
-        return oracle.paged_attention(q, k, v, t, n, "bf16")
-
-    start = time.perf_counter()
-    with concurrent.futures.ThreadPoolExecutor(threads) as pool:
-        list(pool.map(one, inputs))
-    return time.perf_counter() - start
-
-
-def cpu_threads():
+    path = str(ROOT / "baseline" / "_ref")
+    if not (ROOT / "baseline" / "_ref" / "vllm_rlt" / "__init__.py").exists():
+        return None
+    if path not in sys.path:
+        sys.path.insert(0, path)
     try:
-        from threadpoolctl import threadpool_limits
-
-        threadpool_limits(1)  # one BLAS thread per worker; rows run in parallel
-    except ImportError:
-        pass
-    return os.cpu_count() or 1
+        return importlib.import_module(name)
+    except Exception:  # an install that cannot be imported counts as absent
+        return None
 
 
-def sample_rows(plan, target_tokens):
-    order = np.random.default_rng(123).permutation(plan.num_rows)
+class HostDecode:
+    """configs[1] rows on the host, for the reference's own CPU path.
+
+    The selected rows' query-plane pages are laid out in a compact bf16 pool
+    (each row's pages consecutive), filled by tiling a bank of 512 seeded
+    N(0,1) pages: the reference's torch_paged_attention reads every context
+    token of every row once, so its time depends on the shapes only."""
+
+    BANK_PAGES = 512
+
+    def __init__(self, plan, rows, seed=0):
+        import torch
+
+        self.rows = list(rows)
+        page, hkv, d = plan.page, plan.num_kv_heads, plan.head_dim
+        lengths = np.array([int(plan.context_lengths[r]) for r in self.rows], dtype=np.int64)
+        pages = (lengths + page - 1) // page
+        total = int(pages.sum())
+        g = torch.Generator().manual_seed(seed)
+        bank_k = torch.randn((self.BANK_PAGES, page, hkv, d), generator=g).to(torch.bfloat16)
+        bank_v = torch.randn((self.BANK_PAGES, page, hkv, d), generator=g).to(torch.bfloat16)
+        pick = torch.arange(total) % self.BANK_PAGES
+        self.key = bank_k[pick]
+        self.value = bank_v[pick]
+        width = int(pages.max())
+        tables = np.full((len(self.rows), width), -1, dtype=np.int32)
+        first = np.concatenate([[0], np.cumsum(pages)[:-1]])
+        for i, (f, n) in enumerate(zip(first, pages)):
+            tables[i, :n] = np.arange(f, f + n)
+        self.tables = torch.from_numpy(tables)
+        self.lengths = torch.from_numpy(lengths.astype(np.int32))
+        self.q = torch.randn((len(self.rows), plan.num_q_heads, d), generator=g).to(torch.bfloat16)
+        self.tokens = int(lengths.sum())
+        from vllm_rlt_b200.kernels.paged_attention import decode_bytes
+
+        self.bytes = decode_bytes(lengths, plan.num_q_heads, hkv, d, 2, page)
+
+    def run(self, fn):
+        return fn(self.q, self.key, self.value, self.tables, self.lengths)
+
+
+def reference_cpu_path():
+    """(callable, kind, label) of the reference's CPU decode: its own
+    torch_paged_attention (vllm_rlt/kernels/paged_attention.py:12-36) from the
+    unmodified install, else the numpy restatement of it in oracle/."""
+    import torch
+
+    module = reference_module("vllm_rlt.kernels.paged_attention")
+    if module is not None:
+        return module.torch_paged_attention, "reference", \
+            "the reference's torch_paged_attention (baseline/_ref), bf16 inputs, fp32 math"
+    import oracle
+
+    def bits(t):
+        return t.contiguous().view(torch.int16).numpy().view(np.uint16)
+
+    def port(q, k, v, tables, lengths):
+        return oracle.paged_attention(bits(q), bits(k), bits(v), tables.numpy(),
+                                      lengths.numpy(), "bf16")
+
+    return port, "port", "numpy restatement of the reference's torch path (oracle/), " \
+        "the reference install being absent"
+
+
+def reference_cpu_sample(plan, budget_s):
+    """Rows per step for the reference's CPU path: the whole batch when one
+    call fits ``budget_s`` seconds at the rate of a pilot call, else the
+    largest seeded random subset that does. Returns (HostDecode, fn, kind,
+    label, threads)."""
+    import torch
+
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    fn, kind, label = reference_cpu_path()
+    order = [int(r) for r in np.random.default_rng(123).permutation(plan.num_rows)]
+    pilot = HostDecode(plan, order[:8])
+    pilot.run(fn)
+    t0 = time.perf_counter()
+    pilot.run(fn)
+    rate = pilot.tokens / max(time.perf_counter() - t0, 1e-6)  # context tokens per second
     rows, tokens = [], 0
     for r in order:
-        rows.append(int(r))
-        tokens += int(plan.context_lengths[r])
-        if tokens >= target_tokens:
+        n = int(plan.context_lengths[r])
+        if rows and (tokens + n) / rate > budget_s:
             break
-    return rows, tokens
+        rows.append(r)
+        tokens += n
+    return HostDecode(plan, rows), fn, kind, label, threads
+
+
+def reference_kv_cpu(batch=64, reps=20):
+    """BASELINE B4: the reference's CPU KVCacheManager.write (one layer, a
+    batch of rows) and finalize_token (one token, every layer, into the deeper
+    planes) in microseconds per call, Ouro geometry (24 layers, 16 KV heads x
+    128, page 16, 4 planes), bf16 (vllm_rlt/core/kv_cache_manager.py:498-614)."""
+    import torch
+
+    module = reference_module("vllm_rlt.core.kv_cache_manager")
+    if module is None:
+        return {"unavailable": "the reference is not installed under baseline/_ref"}
+    torch.set_num_threads(os.cpu_count() or 1)
+    cache = module.KVCacheManager(num_layers=24, num_kv_heads=16, head_dim=128,
+                                  num_blocks=4 * batch, block_size=16, max_loops=4,
+                                  dtype=torch.bfloat16)
+    ids = [f"r{i}" for i in range(batch)]
+    for rid in ids:
+        cache.allocate(rid, 16)
+    k = torch.randn(batch, 16, 128).to(torch.bfloat16)
+    for layer in range(24):  # position 0 at depth 0 of every layer: finalize may then run
+        cache.write(layer, ids, [0] * batch, [0] * batch, k, k)
+    t0 = time.perf_counter()
+    for i in range(reps):
+        cache.write(i % 24, ids, [0] * batch, [0] * batch, k, k)
+    write_us = (time.perf_counter() - t0) / reps * 1e6
+    t0 = time.perf_counter()
+    for i in range(reps):
+        cache.finalize_token(ids[i % batch], 0, 0)
+    finalize_us = (time.perf_counter() - t0) / reps * 1e6
+    return {"write_us": round(write_us, 1), "write_rows": batch,
+            "finalize_token_us": round(finalize_us, 1),
+            "finalize": "one token: 24 layers x K,V copied from plane 0 into planes 1-3",
+            "threads": torch.get_num_threads(), "kind": "reference"}
 
 
 def run_reference(args):
     from vllm_rlt_b200 import workloads
-    from vllm_rlt_b200.kernels.paged_attention import decode_bytes
 
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return
     plan = workloads.config2_plan(0, rows=args.rows)
-    rows, tokens = sample_rows(plan, 80_000)
-    inputs = host_sample(plan, rows)
-    threads = cpu_threads()
-    step_bytes = decode_bytes([plan.context_lengths[r] for r in rows], 16, 16, 128, 2)
+    # the whole run (warm-up and timed steps) within about three minutes
+    budget = max(1.0, 150.0 / max(args.steps + args.warmup, 1))
+    host, fn, kind, label, threads = reference_cpu_sample(plan, budget)
     for _ in range(args.warmup):
-        time_cpu(inputs, threads)
-    times = [time_cpu(inputs, threads) for _ in range(args.steps)]
+        host.run(fn)
+    times = []
+    for _ in range(args.steps):
+        t0 = time.perf_counter()
+        host.run(fn)
+        times.append(time.perf_counter() - t0)
     total = sum(times)
-    value = step_bytes * args.steps / total / 1e9
-    sample = (f"{len(rows)} of {plan.num_rows} rows per step (sum ctx {tokens}), the reference "
-              "algorithm restated in numpy (oracle/), bf16 inputs, fp32 math")
+    value = host.bytes * args.steps / total / 1e9
+    sample = (f"{len(host.rows)} of {plan.num_rows} rows per step (sum ctx {host.tokens}); "
+              f"{label}; {threads} threads")
     line = {
         "metric": METRIC, "value": round(value, 3), "unit": "GB/s", "impl": "reference",
         "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": round(total / args.steps * 1e3, 3), "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
-        "config": {"workload": WORKLOAD, "sample": sample, "l2": "host run"},
+        "config": {"workload": WORKLOAD, "sample": sample, "l2": "host run",
+                   "same_config": len(host.rows) == plan.num_rows},
         "cpu_baseline": {"value": round(value, 3), "unit": "GB/s", "cores": threads,
-                         "kind": "port", "sample": sample},
+                         "kind": kind, "sample": sample},
         "e2e": {"value": round(value, 3), "unit": "GB/s", "h2d_bytes_per_step": 0,
                 "d2h_bytes_per_step": 0},
+        "reference_kv_cpu": reference_kv_cpu(),
     }
     print(json.dumps(line), flush=True)
 
@@ -508,16 +600,25 @@ def shared_extra(device, steps, warmup, rank):
     }
 
 
-def ouro_extra(device, steps, warmup, rank, requests=64):
+def ouro_extra(device, steps, warmup, rank, world=1, requests=64):
     """random-init Ouro-1.4B-shaped mixed-depth decode. 64 resident
     requests per GPU (LAST-EXITED needs ~1.6 GB of KV per request at 4 planes
     x 24 layers, so 512 requests are reached at 8 GPUs), contexts uniform in
     [256, 4096], per-token exit depth uniform in {1..4}; one step = one
-    CUDA-graph replay of the recurrent core at every request's own depth."""
+    CUDA-graph replay of the recurrent core at every request's own depth.
+
+    With several GPUs every rank is one request-sharded replica, and each step
+    also runs the single front-end's exchange: an NCCL all-gather over NVLink
+    of every rank's sampled tokens and exit flags, copied to pinned host
+    memory without a sync (the front-end reads step t's tokens while step
+    t + 1 runs). The job's rate is the tokens of all ranks over the slowest
+    rank's device time."""
     import torch
+    import torch.distributed as dist
 
     from vllm_rlt_b200.ouro import (DecodeScheduler, OuroDecoder, OuroShape, OuroWeights,
                                     decode_bytes_per_pass)
+    from vllm_rlt_b200.replicas import gather_step_outputs, max_over_ranks
 
     rng = np.random.default_rng(50)  # same request mix on every rank (weak scaling)
     shape = OuroShape()
@@ -532,41 +633,58 @@ def ouro_extra(device, steps, warmup, rank, requests=64):
         for s0 in range(0, flat.numel(), 1 << 30):
             flat[s0 : s0 + (1 << 30)].normal_(generator=g)
     sched = DecodeScheduler(dec, ctx, lambda slot, i: int(exits[slot, i]))
+    front = world > 1 and dist.is_initialized()
+    seen = [torch.empty((world, requests), dtype=torch.int64, pin_memory=True) for _ in range(2)]
+
+    def step(i):
+        exiting = sched.prepare()
+        dec.run()
+        if front:
+            tokens, _flags = gather_step_outputs(dec.tokens, dec.exit_mask)
+            seen[i & 1].copy_(tokens, non_blocking=True)
+        sched.advance(exiting)
+
     exiting = sched.prepare()
     dec.capture()
     dec.run()
     sched.advance(exiting)
-    for _ in range(warmup):
-        exiting = sched.prepare()
-        dec.run()
-        sched.advance(exiting)
+    for i in range(warmup):
+        step(i)
     torch.cuda.synchronize(device)
+    if front:
+        dist.barrier(device_ids=[device.index])
     a = torch.cuda.Event(enable_timing=True)
     b = torch.cuda.Event(enable_timing=True)
     generated0 = sched.generated
     step_bytes = 0
     a.record()
-    for _ in range(steps):
+    for i in range(steps):
         step_bytes += decode_bytes_per_pass(shape, sched.pos + 1)
-        exiting = sched.prepare()
-        dec.run()
-        sched.advance(exiting)
+        step(i)
     b.record()
     torch.cuda.synchronize(device)
     ms = a.elapsed_time(b)
     tokens = sched.generated - generated0
+    (job_ms,), job_tokens = max_over_ranks([ms], float(tokens), device=device)
     errors = dec.attention.check_errors()
     peak, kind = measured_peak()
     gbs = step_bytes / (ms / 1e3) / 1e9
     kv_gb = (dec.key_cache.numel() + dec.value_cache.numel()) * 2 / 1e9
     del dec, weights
     torch.cuda.empty_cache()
+    job_tok_s = job_tokens / (job_ms / 1e3)
     return {
         "workload": "configs[2]: Ouro-1.4B-shaped (24 layers x 4 loops, 2048 hidden, 16x128 "
                     "heads, SwiGLU 5632, vocab 49152, RoPE 1e4, bf16, random init), 64 requests "
                     "per GPU, ctx U[256,4096], exit depth U{1..4}, LAST-EXITED, graph-captured step",
-        "tok_s_per_gpu": round(tokens / (ms / 1e3), 1), "tokens": int(tokens),
-        "steps": steps, "ms_per_step": round(ms / steps, 3),
+        "n_gpus": world,
+        "job_tok_s": round(job_tok_s, 1),
+        "tok_s_per_gpu": round(job_tok_s / world, 1),
+        "tok_s_rank0": round(tokens / (ms / 1e3), 1),
+        "tokens": int(job_tokens), "steps": steps, "ms_per_step": round(job_ms / steps, 3),
+        "timing": "CUDA events per rank, max over ranks; tokens summed over ranks",
+        "front_end_gather": ("NCCL all-gather of sampled tokens + exit flags every step, "
+                             "async copy to pinned host") if front else None,
         "kv_pool_gb": round(kv_gb, 1),
         "hbm": {"achieved": round(gbs, 1), "peak": peak, "unit": "GB/s",
                 "frac": round(gbs / peak, 4), "peak_kind": kind,
@@ -601,7 +719,7 @@ def run_ours(args):
         if args.workload == "prefill":
             res = prefill_extra(device, args.steps, args.warmup, rank)
         elif args.workload == "ouro":
-            res = ouro_extra(device, args.steps, args.warmup, rank)
+            res = ouro_extra(device, args.steps, args.warmup, rank, world)
         elif args.workload == "shared":
             res = shared_extra(device, args.steps, args.warmup, rank)
         else:
@@ -753,28 +871,29 @@ def run_ours(args):
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        rows, tokens = sample_rows(plan, 80_000)
-        inputs = host_sample(plan, rows)
-        threads = cpu_threads()
-        sample_bytes = decode_bytes([plan.context_lengths[r] for r in rows], 16, 16, 128, 2)
-        time_cpu(inputs[:2], threads)
+        host, fn, kind, label, threads = reference_cpu_sample(plan, 5.0)
+        host.run(fn)
         reps, spent = 0, 0.0
-        while spent < 10.0 and reps < 50:
-            spent += time_cpu(inputs, threads)
+        while spent < 12.0 and reps < 20:
+            t_start = time.perf_counter()
+            host.run(fn)
+            spent += time.perf_counter() - t_start
             reps += 1
         cpu = {
-            "value": round(sample_bytes * reps / spent / 1e9, 3), "unit": "GB/s",
-            "cores": threads, "kind": "port",
-            "sample": (f"{len(rows)} of {plan.num_rows} rows (sum ctx {tokens}) x {reps} reps, "
-                       "numpy restatement of the reference's torch path, fp32 math"),
+            "value": round(host.bytes * reps / spent / 1e9, 3), "unit": "GB/s",
+            "cores": threads, "kind": kind,
+            "sample": (f"{len(host.rows)} of {plan.num_rows} rows (sum ctx {host.tokens}) x "
+                       f"{reps} calls; {label}"),
+            "reference_kv_cpu": reference_kv_cpu(),
         }
+        del host
 
     extras = {}
     if not args.no_extras:
         # free the decode pool first: the extras allocate their own pools
         del kpool, vpool, k_layer, v_layer
         torch.cuda.empty_cache()
-        for name, fn in (("ouro", lambda: ouro_extra(device, 30, 3, rank)),
+        for name, fn in (("ouro", lambda: ouro_extra(device, 30, 3, rank, world)),
                          ("prefill", lambda: prefill_extra(device, 10, 3, rank)),
                          ("longctx", lambda: longctx_extra(device, 20, 5, rank, world)),
                          ("shared_prefix", lambda: shared_extra(device, 20, 5, rank))):

@@ -205,11 +205,17 @@ int rlt_paged_decode_shared(const void* q, const void* key_cache, const void* va
  * every GPU using this entry point holds until the process exits. It calls no
  * cudaMalloc/cudaFree or other allocating routine.
  *  - The first call on a device looks up that device's copy of the array
- *    (with the device current); make that first call before any stream
- *    capture on the device.
- *  - Returns RLT_E_SCRATCH, launching nothing, when the launch shape needs
- *    more than the array holds: rlt_paged_decode_workspace_bytes(num_rows,
- *    num_q_heads, head_dim, page_size, table_width) > RLT_NOALLOC_SCRATCH_BYTES.
+ *    (with the device current), and under lazy module loading it is also the
+ *    moment the driver places the array: make that first call at start-up,
+ *    before any stream capture on the device. The looked-up address is kept
+ *    for the life of the process, so the device must not be reset
+ *    (cudaDeviceReset) while the library is in use.
+ *  - Returns RLT_E_SCRATCH, launching nothing, when a launch that splits rows
+ *    (the 16-byte-vector path: head_dim 32/64/128/256 with 16-byte aligned
+ *    strides) needs more split partials than the array holds, i.e. when
+ *    rlt_paged_decode_workspace_bytes(num_rows, num_q_heads, head_dim,
+ *    page_size, table_width) > RLT_NOALLOC_SCRATCH_BYTES. Other shapes run
+ *    without splits and use none of the array, at any size.
  *  - All calls share the array; calls that overlap on the GPU race on it, so
  *    serialise them (one stream, or events between streams).
  * This entry point has no counterpart in the reference, which always

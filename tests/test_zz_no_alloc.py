@@ -18,6 +18,7 @@ import numpy as np
 import pytest
 import torch
 
+import oracle
 from helpers import assert_close
 from vllm_rlt_b200 import _lib
 
@@ -94,6 +95,13 @@ def test_no_alloc_matches_workspace_entry_point_on_two_calls():
     for a, b in zip(got, expected):
         assert_close(to_u16(a), to_u16(b), "bf16")
         assert torch.equal(a, b)  # same kernels and split plan: identical bits
+    # and directly against the CPU oracle for a few rows of the second call
+    rows = [0, 7, 23]
+    x = second
+    want = oracle.paged_attention(to_u16(x["q"][rows]), to_u16(x["k"]), to_u16(x["v"]),
+                                  x["tables"][rows].cpu().numpy(),
+                                  x["lengths"][rows].cpu().numpy(), "bf16")
+    assert_close(to_u16(got[1][rows]), want, "bf16")
 
 
 def test_no_alloc_refuses_shapes_beyond_its_static_scratch():

@@ -10,12 +10,20 @@
 // caller-provided workspace.
 //
 // The array is a fixed 16 MiB per GPU that loads this part of the library and
-// stays allocated until the process exits. All calls share it and it keeps
-// the previous call's contents: each call clears the split counters it needs
-// at zero (a memset on the call's stream) and reads only split partials it
-// wrote itself. Two calls that overlap on the GPU (different streams, or
-// different host threads on the same device) race on the array: serialise
-// them.
+// stays allocated until the process exits. The driver places it when the
+// library's device code is loaded on a device; under lazy module loading
+// (CUDA_MODULE_LOADING=LAZY) that happens at the first call on the device, so
+// make that call at start-up. All calls share the array and it keeps the
+// previous call's contents: each call's first kernel (the one-CTA split
+// schedule, on the call's stream) resets the split counters before the
+// decode kernel uses them, and a call reads only split partials it wrote
+// itself. Two calls that overlap on the GPU (different streams, or different
+// host threads on the same device) race on the array: serialise them.
+//
+// The device address of the array is looked up once per device and cached
+// for the life of the process; this assumes the device is not reset
+// (cudaDeviceReset) while the library is in use, since a reset unloads the
+// module and the array may come back elsewhere.
 #include <mutex>
 
 #include "common.cuh"
