@@ -63,7 +63,8 @@ def parse():
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--no-extras", action="store_true",
                    help="skip the Ouro, prefill, long-context and shared-prefix sub-measurements")
-    p.add_argument("--workload", choices=["decode", "prefill", "longctx", "ouro", "shared"],
+    p.add_argument("--workload",
+                   choices=["decode", "prefill", "longctx", "ouro", "shared", "kernels"],
                    default="decode",
                    help="decode: the headline line; the others: that workload alone")
     return p.parse_args()
@@ -693,6 +694,173 @@ def ouro_extra(device, steps, warmup, rank, world=1, requests=64):
     }
 
 
+def kernels_extra(device, steps, warmup):
+    """Every auxiliary kernel of the path once at a representative size, timed
+    with CUDA events (median of ``steps`` launches after ``warmup``): the
+    algorithmic bytes each moves, and GB/s against the copy peak. Sizes: Ouro
+    geometry (24 layers, 16 KV heads x 128, page 16, 4 planes, hidden 2048,
+    SwiGLU 5632), bf16; a 2048-token prefill chunk for the page write and the
+    per-row glue, 512 exiting tokens for the exit copy, a 512-row routing
+    bank, 256 Ouro-shaped blocks for the PD page transport (same GPU)."""
+    import torch
+
+    import vllm_rlt_b200 as rb
+    from vllm_rlt_b200.kernels import ouro_ops
+    from vllm_rlt_b200.pd import PageTransport
+
+    g = torch.Generator(device=device).manual_seed(5)
+    bf = torch.bfloat16
+    layers, hkv, d, page, planes, hidden, inter = 24, 16, 128, 16, 4, 2048, 5632
+    rng = np.random.default_rng(5)
+    results = {}
+    peak, kind = measured_peak()
+
+    def timed(name, fn, nbytes, note):
+        for _ in range(warmup):
+            fn()
+        torch.cuda.synchronize(device)
+        times = []
+        for _ in range(steps):
+            a = torch.cuda.Event(enable_timing=True)
+            b = torch.cuda.Event(enable_timing=True)
+            a.record()
+            fn()
+            b.record()
+            b.synchronize()
+            times.append(a.elapsed_time(b))
+        us = statistics.median(times) * 1e3
+        gbs = nbytes / (us / 1e6) / 1e9
+        results[name] = {"us": round(us, 2), "bytes": int(nbytes), "gb_s": round(gbs, 1),
+                         "frac_of_peak": round(gbs / peak, 4), "what": note}
+
+    # pool: 1,200 blocks of 24 layers (K and V: 3.5 GB)
+    blocks = 1200
+    kc = torch.empty((blocks, layers, page, hkv, d), device=device, dtype=bf)
+    vc = torch.empty_like(kc)
+    fill_random(kc, g)
+    fill_random(vc, g)
+    row_bytes = hkv * d * 2
+
+    # KV page write: a 2048-token chunk into one layer
+    n = 2048
+    slots = torch.from_numpy(rng.permutation(blocks * page)[:n]).to(device)
+    wb, wo = slots // page, slots % page
+    k = torch.randn((n, hkv, d), generator=g, device=device).to(bf)
+    v = torch.randn_like(k)
+    timed("kv_write_kernel", lambda: rb.write_kv(kc, vc, 3, wb, wo, k, v), 2 * 2 * n * row_bytes,
+          "2048 rows x (K, V) of 16x128 bf16 into one layer: read + write")
+
+    # exit copy: 512 tokens leaving at depth 0 -> planes 1..3, all 24 layers;
+    # slot s owns one page per plane, tokens at distinct (page, offset)
+    exiting = 512
+    tables = np.zeros((exiting, planes, 1), dtype=np.int32)
+    for s_ in range(exiting):
+        for pl in range(planes):
+            tables[s_, pl, 0] = (s_ // page) * planes + pl
+    tables_t = torch.from_numpy(tables).to(device)
+    desc = torch.zeros((exiting, 3), dtype=torch.int64)
+    desc[:, 0] = torch.arange(exiting)
+    desc[:, 2] = torch.arange(exiting) % page
+    desc_t = desc.to(device)
+    timed("finalize_kernel", lambda: rb.finalize(desc_t, tables_t, kc, vc),
+          exiting * 2 * layers * row_bytes * (1 + (planes - 1)),
+          "512 exiting tokens, depth 0 -> 3 deeper planes, 24 layers, K and V: "
+          "each source row read once, written 3 times")
+
+    # routing metadata: a 512-row bank over resident tables [512, 4, 256]
+    rows, width = 512, 256
+    res_tables = torch.from_numpy(rng.integers(0, blocks, size=(rows, planes, width),
+                                               dtype=np.int32)).to(device)
+    mdesc = torch.zeros((rows, 3), dtype=torch.int64)
+    mdesc[:, 0] = torch.arange(rows)
+    mdesc[:, 1] = torch.from_numpy(rng.integers(0, planes, size=rows))
+    mdesc[:, 2] = torch.from_numpy(rng.integers(0, width * page, size=rows))
+    mdesc_t = mdesc.to(device)
+    i64 = dict(device=device, dtype=torch.int64)
+    outs = [torch.empty(rows, **i64) for _ in range(2)]
+    lens = torch.empty(rows, device=device, dtype=torch.int32)
+    ob, oo = torch.empty(rows, **i64), torch.empty(rows, **i64)
+    out_tables = torch.empty((rows, width), device=device, dtype=torch.int32)
+    timed("metadata_kernel",
+          lambda: rb.metadata(mdesc_t, res_tables, outs[0], outs[1], lens, ob, oo, out_tables,
+                              rows, rows, page, planes, width),
+          rows * (24 + 4 * width + 4 * width + 8 * 4 + 4),
+          "512-row bank: descriptor, the row's plane table read and copied, 4 int64 + 1 int32 "
+          "outputs per row")
+
+    # resident hidden-state gather / scatter: 512 rows x 2048 bf16
+    pool = torch.randn((rows, hidden), generator=g, device=device).to(bf)
+    perm_slots = torch.from_numpy(rng.permutation(rows)).to(device)
+    hid = torch.empty((rows, hidden), device=device, dtype=bf)
+    timed("gather_kernel", lambda: rb.gather(pool, perm_slots, hid, rows, rows),
+          2 * rows * hidden * 2, "512 rows x 2048 bf16: read + write")
+    timed("scatter_kernel", lambda: rb.scatter(hid, perm_slots, pool, rows),
+          2 * rows * hidden * 2, "512 rows x 2048 bf16: read + write")
+
+    # packed-prefill metadata: stage 64K int64 values, expand 2048 tokens
+    vals = 1 << 16
+    src = torch.from_numpy(rng.integers(0, 1000, size=vals)).pin_memory()
+    t64 = torch.empty(vals, **i64)
+    t32 = torch.empty(vals, device=device, dtype=torch.int32)
+    timed("stage_kernel", lambda: rb.stage_prefill(src, t64, t32, vals),
+          vals * (8 + 8 + 4), "65,536 int64 from mapped pinned host memory -> int64 + int32")
+    pos = torch.from_numpy(rng.integers(0, width * page, size=n)).to(device)
+    seqs = torch.from_numpy(rng.integers(0, 16, size=n)).to(device)
+    ptab = torch.from_numpy(rng.integers(0, blocks, size=(16, width), dtype=np.int32)).to(device)
+    eb, eo = torch.empty(n, **i64), torch.empty(n, **i64)
+    timed("expand_kernel", lambda: rb.expand_prefill(pos, seqs, ptab, eb, eo, n, width, page),
+          n * (8 + 8 + 4 + 8 + 8), "2048 tokens: position, sequence, table entry in; block, "
+                                   "offset out")
+
+    # RoPE + page write: 2048 rows of fused qkv [2048, (16 + 32) x 128]
+    qkv = torch.randn((n, 48 * d), generator=g, device=device).to(bf)
+    rpos = torch.from_numpy(rng.integers(0, 4096, size=n)).to(device)
+    inv_freq = 1.0 / (10000.0 ** (torch.arange(0, d, 2, device=device, dtype=torch.float32) / d))
+    timed("rope_write_kernel",
+          lambda: ouro_ops.rope_write_kv(qkv, rpos, inv_freq, kc, vc, 5, wb, wo, 16, 16, d),
+          n * (48 * d * 2 + 16 * d * 2 + 2 * row_bytes + 8 * 3),
+          "2048 rows: qkv read, rotated q written, rotated k and v written into the pages")
+
+    # paired RMSNorm with residual, SwiGLU
+    x = torch.randn((n, hidden), generator=g, device=device).to(bf)
+    res = torch.randn_like(x)
+    w1 = torch.ones(hidden, device=device, dtype=bf)
+    timed("rms_norm_vec_kernel",
+          lambda: ouro_ops.rms_norm(x, w1, 1e-6, residual=res, weight2=w1),
+          n * hidden * 2 * 4, "2048 x 2048 bf16: x and residual read, two normed outputs written")
+    gu = torch.randn((n, 2 * inter), generator=g, device=device).to(bf)
+    timed("silu_mul_vec_kernel", lambda: ouro_ops.silu_mul(gu, inter),
+          n * inter * 2 * 3, "2048 x 11264 bf16 read, 2048 x 5632 written")
+
+    # PD page transport on one GPU: 256 whole Ouro-shaped blocks, 4 planes
+    del k, v, qkv, gu, x, res
+    src_k, src_v = kc[:512], vc[:512]
+    dst_k, dst_v = kc[512:1024], vc[512:1024]
+    transport = PageTransport(src_k, src_v, page, transfer_chunk_bytes=1 << 30,
+                              max_inflight_bytes=1 << 34)
+    transport.connect("peer", dst_k, dst_v)
+    local = [list(map(int, rng.permutation(512)[:64])) for _ in range(planes)]
+    remote = [list(map(int, rng.permutation(512)[:64])) for _ in range(planes)]
+
+    def transfer():
+        transport.poll()  # retire the previous (completed) transfer from the budget
+        transport.stream.wait_stream(torch.cuda.current_stream(device))
+        if not transport.submit("t", 0, "peer", local, remote, 0, 64 * page):
+            raise RuntimeError("the PD transfer was refused by the in-flight budget")
+        torch.cuda.current_stream(device).wait_stream(transport.stream)
+
+    timed("copy_segments_kernel", transfer,
+          2 * planes * 64 * 2 * layers * page * row_bytes,
+          "256 whole blocks (4 planes x 64 pages, 24 layers, K and V): read + write")
+    torch.cuda.synchronize(device)
+    transport.poll()
+    errors = rb.B200PagedAttention(device, bf, d, page).check_errors()
+    del kc, vc
+    torch.cuda.empty_cache()
+    return {"kernels": results, "peak": peak, "peak_kind": kind, "errors": errors,
+            "timing": "CUDA events per launch, median"}
+
+
 # ------------------------------------------------------------------ ours
 
 
@@ -722,6 +890,8 @@ def run_ours(args):
             res = ouro_extra(device, args.steps, args.warmup, rank, world)
         elif args.workload == "shared":
             res = shared_extra(device, args.steps, args.warmup, rank)
+        elif args.workload == "kernels":
+            res = kernels_extra(device, args.steps, args.warmup)
         else:
             res = longctx_extra(device, args.steps, args.warmup, rank, world)
         if world > 1:

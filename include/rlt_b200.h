@@ -193,6 +193,41 @@ int rlt_paged_decode_shared(const void* q, const void* key_cache, const void* va
                             int64_t out_row_stride, int64_t out_head_stride, float scale,
                             void* stream);
 
+/* rlt_paged_decode_shared with its two launches selectable: phases = 1 runs
+ * only the prefix-chunk partials (they need neither `out` nor `suffix_lse`,
+ * so they may run on another stream while rlt_paged_decode_lse computes the
+ * suffixes), 2 only their merge into `out`, 3 both (= rlt_paged_decode_shared).
+ * Same arguments otherwise. No counterpart in the reference. */
+int rlt_paged_decode_shared_phases(const void* q, const void* key_cache, const void* value_cache,
+                                   const int32_t* block_tables, const int32_t* chunks,
+                                   const int32_t* members, const int32_t* member_slots,
+                                   const int32_t* row_slots, const float* suffix_lse, void* out,
+                                   void* workspace, size_t workspace_bytes, int32_t* status,
+                                   int32_t dtype, int32_t num_rows, int32_t num_q_heads,
+                                   int32_t num_kv_heads, int32_t head_dim, int32_t page_size,
+                                   int32_t table_width, int64_t num_blocks, int32_t num_chunks,
+                                   int32_t num_slots, int32_t num_members, int64_t q_row_stride,
+                                   int64_t q_head_stride, int64_t k_block_stride,
+                                   int64_t k_token_stride, int64_t k_head_stride,
+                                   int64_t v_block_stride, int64_t v_token_stride,
+                                   int64_t v_head_stride, int64_t table_row_stride,
+                                   int64_t out_row_stride, int64_t out_head_stride, float scale,
+                                   int32_t phases, void* stream);
+
+/* Per-call suffix metadata of the shared-prefix decode, built on the device
+ * from the call's own block tables and context lengths, so a plan made once
+ * for a batch stays valid while its rows grow (decode steps, CUDA-graph
+ * replays): suffix_tables[r] = block_tables[r] shifted past prefix_pages[r]
+ * pages and padded with -1 (row stride table_width), suffix_lengths[r] =
+ * context_lengths[r] - prefix_pages[r] * page_size. A row whose context no
+ * longer covers its shared pages gets an empty suffix and raises status bit 1
+ * (its plan is stale). One launch. No counterpart in the reference. */
+int rlt_shared_prefix_suffix(const int32_t* block_tables, const int32_t* context_lengths,
+                             const int32_t* prefix_pages, int32_t* suffix_tables,
+                             int32_t* suffix_lengths, int32_t* status, int32_t num_rows,
+                             int32_t table_width, int32_t page_size, int64_t table_row_stride,
+                             void* stream);
+
 /* Size of the static split-KV scratch of rlt_paged_decode_noalloc (bytes). */
 #define RLT_NOALLOC_SCRATCH_BYTES (16u << 20)
 

@@ -44,12 +44,21 @@ def test_host_only_entry_points_without_gpu():
     assert lib.rlt_version() >= 100
     # no split can be needed when every row fits one split
     assert lib.rlt_paged_decode_workspace_bytes(8, 16, 128, 16, 16) == 0
-    # graph width 4096 x page 16: up to 128 splits of fp32 (acc + max + sum),
-    # after the int metadata -- one merge counter per (row, query head), the
-    # rows + 1 work schedule and the claim counter -- rounded to 16 bytes
-    meta = (256 * 16 + 256 + 2) * 4
-    assert lib.rlt_paged_decode_workspace_bytes(256, 16, 128, 16, 4096) == (
-        (meta + 15) // 16 * 16 + 256 * 128 * 16 * 130 * 4)
+    # The reference's graph width 4096 x page 16 allows 128 splits per row;
+    # split partials (fp32 acc + max + sum per query head) live in a ring of
+    # max(2 x 128, 1024) (row, split) slots, not rows x 128. Before them the
+    # int metadata: one merge counter per (row, query head), the rows + 1
+    # work schedule, the claim counter, the row order, each row's first ring
+    # pair, per-row merge counts and one sequence word per ring slot,
+    # rounded to 16 bytes.
+    def expected(rows, ring):
+        meta = (rows * 16 + 4 * rows + 2 + ring) * 4
+        return (meta + 15) // 16 * 16 + ring * 16 * 130 * 4
+
+    assert lib.rlt_paged_decode_workspace_bytes(256, 16, 128, 16, 4096) == expected(256, 1024)
+    assert lib.rlt_paged_decode_workspace_bytes(256, 16, 128, 16, 4096) < 9 << 20
+    # few rows: one slot per possible (row, split), no ring wrap-around
+    assert lib.rlt_paged_decode_workspace_bytes(4, 16, 128, 16, 4096) == expected(4, 4 * 128)
     assert lib.rlt_paged_prefill_workspace_bytes(0, 16, 128, 16, 64) == 0
 
 

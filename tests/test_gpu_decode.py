@@ -17,7 +17,7 @@ import oracle
 import vllm_rlt_b200 as rb
 from gpu_helpers import TORCH, CudaWriter, to_numpy, to_torch
 from helpers import assert_close, digest, load, query_inputs, replay_pool, scenario_names
-from vllm_rlt_b200 import workloads
+from vllm_rlt_b200 import _lib, workloads
 
 pytestmark = pytest.mark.gpu
 
@@ -248,3 +248,17 @@ def test_config2_subset_vs_oracle_and_properties():
     assert_close(to_numpy(out[rows]), expected, "bf16")
     again = rb.paged_attention(q, key[:, 0], value[:, 0], tables, lengths)
     torch.testing.assert_close(again, out, rtol=0, atol=0)  # deterministic
+
+
+def test_status_word_first_made_under_inference_mode_can_be_cleared():
+    """The reference's graph runner calls the backend under
+    torch.inference_mode; the per-device status word it may create there must
+    stay an ordinary tensor that a later check outside that mode can clear."""
+    device = torch.device("cuda", 0)
+    _lib._status.pop(0, None)
+    with torch.inference_mode():
+        word = _lib.status_word(device)
+        word.fill_(2)
+    assert not word.is_inference()
+    assert _lib.read_status(device) == [_lib.STATUS_BITS[2]]
+    assert _lib.read_status(device) == []

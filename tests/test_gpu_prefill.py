@@ -89,9 +89,14 @@ def test_chunked_prefill_with_prefix_reuse_vs_oracle(dtype):
 
 # The reference's own bound for its tensor-core prefill (FA4, which rounds P
 # to the input dtype before the PV product) against the fp32 torch path:
-# tests/test_flash_attention.py:66-67 and :187-188.
-FA4_TOLERANCE = {"bf16": dict(atol=0.015, rtol=0.02, ulps=0),
-                 "f16": dict(atol=0.002, rtol=0.02, ulps=0)}
+# tests/test_flash_attention.py:66-67 and :187-188. Kernel versions 1-5 round
+# P to bf16 the same way; on these cases their largest bf16 error is 2.4e-3
+# beyond one output ulp (a query row that attends only four keys), so they
+# are held to this bound for bf16. Versions 6 and 7, which split P into a bf16
+# hi + lo pair where few keys are attended (6) or everywhere (7), and every
+# fp16 version are held to the stated bound: max-abs 2e-3 plus one ulp.
+FA4_TOLERANCE = {"bf16": dict(atol=0.015, rtol=0.02, ulps=0), "f16": {}}
+ROUNDED_P_VERSIONS = (1, 2, 3, 4, 5)
 
 
 def _with_version(version, fn):
@@ -112,17 +117,24 @@ def test_each_tensor_core_kernel_vs_oracle(dtype, page):
     shared memory; 3: two tiles, P in TMEM; 4: as 3 with each row's softmax
     split over two warps by key-column half; 5: as 3 with the softmax
     warpgroups' registers raised so a row's scores stay in registers for one
-    pass) on long chunks that run many key tiles, with ragged tails and a
-    chunk shorter than one tile. Kernels 2 and 3 differ only in where P is
-    held, so their outputs are bit-identical."""
+    pass; 6: as 5 with bf16 P split into hi + lo in query tiles whose rows
+    attend fewer than 512 keys; 7: as 6 in every tile) on long chunks that
+    run many key tiles, with ragged tails and a chunk shorter than one tile.
+    Kernels 2 and 3 differ only in where P is held, so their outputs are
+    bit-identical."""
     case = dict(page=page, seed=11, prompt=(1500, 2100, 90, 777), prefix=(0, 700, 30, 1),
                 chunk_cap=1100)
     outs = {}
-    for version in (1, 2, 3, 4, 5):
+    for version in (1, 2, 3, 4, 5, 6, 7):
         out, expected = _with_version(version, lambda: _prefix_reuse_case(dtype, **case))
-        assert_close(to_numpy(out), expected, dtype, **FA4_TOLERANCE[dtype])
+        if version in ROUNDED_P_VERSIONS:
+            assert_close(to_numpy(out), expected, dtype, **FA4_TOLERANCE[dtype])
+        else:
+            assert_close(to_numpy(out), expected, dtype)
         outs[version] = out
     assert torch.equal(outs[2], outs[3])
+    if dtype == "f16":  # fp16's P is never split: 6 and 7 are 5
+        assert torch.equal(outs[5], outs[6]) and torch.equal(outs[5], outs[7])
 
 
 @pytest.mark.parametrize("dtype,d,group", [("bf16", 128, 1), ("f16", 128, 2), ("f32", 64, 1)])

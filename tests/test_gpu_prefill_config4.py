@@ -95,8 +95,26 @@ def oracle_rows(plan, key, value, r, out, seq, rng):
     return got, expected
 
 
-def test_config4_prefill_matches_oracle_on_sampled_rows():
-    plan, key, value, rounds = config4_case()
+@pytest.fixture(scope="module")
+def case():
+    return config4_case()
+
+
+@pytest.mark.parametrize("version", [0, 5, 7])
+def test_config4_prefill_matches_oracle_on_sampled_rows(case, version):
+    """version 0: the library's default kernel; 5: P rounded to bf16; 7: P
+    split into a bf16 hi + lo pair everywhere."""
+    lib = _lib.load()
+    previous = lib.rlt_prefill_tc_select(version) if version else None
+    try:
+        check_config4(case)
+    finally:
+        if previous is not None:
+            lib.rlt_prefill_tc_select(previous)
+
+
+def check_config4(case):
+    plan, key, value, rounds = case
     assert _lib.load().rlt_paged_prefill_uses_tensor_cores(_lib.BF16, 128, 16) == 1
     picks = sampled_sequences(plan)
     rng = np.random.default_rng(11)

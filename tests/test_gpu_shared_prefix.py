@@ -16,6 +16,7 @@ import vllm_rlt_b200 as rb
 from gpu_helpers import TORCH, to_numpy
 from helpers import assert_close
 from test_shared_prefix_plan import make_case
+from vllm_rlt_b200 import _lib
 
 pytestmark = pytest.mark.gpu
 
@@ -113,3 +114,81 @@ def test_decode_log_sum_exp(dtype):
         s = np.einsum("hd,thd->ht", qf[r], k) / np.sqrt(128)
         want = np.log2(np.exp(s - s.max(axis=1, keepdims=True)).sum(axis=1)) + s.max(axis=1) / np.log(2)
         np.testing.assert_allclose(lse[r].cpu().numpy(), want, rtol=0, atol=2e-4)
+
+
+def test_plan_stays_valid_as_rows_grow_and_replays_in_a_graph():
+    """A plan made once keeps serving the batch while its rows grow (each
+    call derives the suffix tables and lengths on the device): decode steps
+    that append tokens -- within the rows' pages and onto fresh pages --
+    eagerly and as replays of one captured CUDA graph whose length and table
+    buffers are updated in place."""
+    page, hkv, d = 16, 4, 128
+    tables, lengths, num_blocks = make_case(21, page=page, rows=10, width=30,
+                                            groups=((0, 1, 2, 3), (5, 6, 7)), shared=(6, 4))
+    lengths = np.minimum(lengths, 20 * page).astype(np.int32)  # room to grow
+    for r in range(10):  # drop table entries beyond the (shortened) context
+        tables[r, -(-int(lengths[r]) // page):] = -1
+    spare = iter(range(num_blocks, num_blocks + 10 * 30))  # fresh pages appended on growth
+    pool_blocks = num_blocks + 10 * 30
+    g = torch.Generator(device="cuda").manual_seed(4)
+    key = torch.randn(pool_blocks, page, hkv, d, generator=g, device="cuda").to(torch.bfloat16)
+    value = torch.randn(pool_blocks, page, hkv, d, generator=g, device="cuda").to(torch.bfloat16)
+    q = torch.randn(10, hkv, d, generator=g, device="cuda").to(torch.bfloat16)
+    plan = rb.plan_shared_prefix(tables, lengths, page, hkv, hkv, "cuda", chunk_tokens=64)
+    t = torch.from_numpy(tables).cuda()
+    n = torch.from_numpy(lengths).cuda()
+    out = torch.empty_like(q)
+    backend = rb.B200PagedAttention("cuda", torch.bfloat16, d, page)
+
+    def grow(steps):
+        for _ in range(steps):
+            for r in range(10):
+                if lengths[r] % page == 0:
+                    tables[r, lengths[r] // page] = next(spare)
+                lengths[r] += 1
+
+    def check():
+        torch.cuda.synchronize()
+        assert backend.check_errors() == []
+        want = oracle.paged_attention(to_numpy(q), to_numpy(key), to_numpy(value), tables,
+                                      lengths, "bf16")
+        assert_close(to_numpy(out), want, "bf16")
+
+    rb.paged_attention_shared(q, key, value, t, plan, context_lengths=n, out=out)
+    check()
+    grow(17)  # eager, a plan from 17 steps ago
+    t.copy_(torch.from_numpy(tables))
+    n.copy_(torch.from_numpy(lengths))
+    rb.paged_attention_shared(q, key, value, t, plan, context_lengths=n, out=out)
+    check()
+    stream = torch.cuda.Stream()
+    stream.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(stream):
+        rb.paged_attention_shared(q, key, value, t, plan, context_lengths=n, out=out)
+    torch.cuda.current_stream().wait_stream(stream)
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        rb.paged_attention_shared(q, key, value, t, plan, context_lengths=n, out=out)
+    for steps in (1, 15, 3):
+        grow(steps)
+        t.copy_(torch.from_numpy(tables))
+        n.copy_(torch.from_numpy(lengths))
+        graph.replay()
+        check()
+
+
+def test_stale_plan_is_reported():
+    """A row whose context shrank below its shared pages is outside the plan:
+    the call flags it (status bit 1) instead of reading past the context."""
+    tables, lengths, num_blocks = make_case(2, rows=6, width=16, groups=((0, 1, 2),), shared=(5,))
+    g = torch.Generator(device="cuda").manual_seed(5)
+    key = torch.randn(num_blocks, 16, 2, 64, generator=g, device="cuda").to(torch.bfloat16)
+    q = torch.randn(6, 2, 64, generator=g, device="cuda").to(torch.bfloat16)
+    plan = rb.plan_shared_prefix(tables, lengths, 16, 2, 2, "cuda")
+    shrunk = lengths.copy()
+    shrunk[1] = 3 * 16  # below the group's 5 shared pages
+    backend = rb.B200PagedAttention("cuda", torch.bfloat16, 64, 16)
+    rb.paged_attention_shared(q, key, key, torch.from_numpy(tables).cuda(), plan,
+                              context_lengths=torch.from_numpy(shrunk).cuda())
+    torch.cuda.synchronize()
+    assert backend.check_errors() == [_lib.STATUS_BITS[1]]

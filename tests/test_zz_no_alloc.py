@@ -106,9 +106,10 @@ def test_no_alloc_matches_workspace_entry_point_on_two_calls():
 
 def test_no_alloc_refuses_shapes_beyond_its_static_scratch():
     lib = _lib.load()
-    # 256 rows at table width 512 (page 16) would need 68 MB of split partials.
-    x = make_inputs(3, 256, [100] * 256, width=512)
-    assert lib.rlt_paged_decode_workspace_bytes(256, 16, 128, 16, 512) > 16 << 20
+    # 64 query heads of head_dim 256 at table width 512 (page 16): the ring of
+    # split partials (1024 slots x 64 heads x 258 fp32) needs 68 MB.
+    x = make_inputs(3, 64, [100] * 64, hq=64, hkv=8, d=256, width=512)
+    assert lib.rlt_paged_decode_workspace_bytes(64, 64, 256, 16, 512) > 16 << 20
     out = torch.zeros_like(x["q"])
     assert decode_no_alloc(lib, x, out) == RLT_E_SCRATCH
     torch.cuda.synchronize()

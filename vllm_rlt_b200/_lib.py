@@ -37,7 +37,7 @@ STATUS_BITS = {
     4: "in-page offset outside [0, page)",
     8: "descriptor slot/depth/position outside the resident tables",
     16: "packed-prefill metadata inconsistent",
-    32: "a bounded wait in a tensor-core kernel timed out",
+    32: "a bounded wait in a kernel timed out (the call's output is void)",
     64: "a tensor-core kernel found its shared memory misaligned",
 }
 
@@ -80,6 +80,12 @@ SIGNATURES = {
         _i32,
         [_p] * 11 + [_sz, _p] + [_i32] * 7 + [_i64] + [_i32] * 3 + [_i64] * 11 + [_f32, _p],
     ),
+    "rlt_paged_decode_shared_phases": (
+        _i32,
+        [_p] * 11 + [_sz, _p] + [_i32] * 7 + [_i64] + [_i32] * 3 + [_i64] * 11
+        + [_f32, _i32, _p],
+    ),
+    "rlt_shared_prefix_suffix": (_i32, [_p] * 6 + [_i32] * 3 + [_i64, _p]),
     "rlt_kv_write": (_i32, [_p] * 7 + [_i32] * 6 + [_i64] * 9 + [_p]),
     "rlt_finalize": (_i32, [_p] * 5 + [_i32] * 8 + [_i64] * 4 + [_p]),
     "rlt_metadata": (_i32, [_p] * 9 + [_i32] * 7 + [_p]),
@@ -144,7 +150,10 @@ def status_word(device: torch.device) -> torch.Tensor:
     index = device.index if device.index is not None else torch.cuda.current_device()
     word = _status.get(index)
     if word is None:
-        word = torch.zeros(1, dtype=torch.int32, device=torch.device("cuda", index))
+        # a normal tensor even when first requested under torch.inference_mode
+        # (the reference's graph runner runs there), so it can be cleared later
+        with torch.inference_mode(False):
+            word = torch.zeros(1, dtype=torch.int32, device=torch.device("cuda", index))
         _status[index] = word
     return word
 

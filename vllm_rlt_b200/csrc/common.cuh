@@ -24,6 +24,17 @@ constexpr int32_t kStatusBadBlock = 2;    // block id outside [0, num_blocks)
 constexpr int32_t kStatusBadOffset = 4;   // in-page offset outside [0, page)
 constexpr int32_t kStatusBadSlot = 8;     // descriptor slot / depth outside the resident tables
 constexpr int32_t kStatusBadSequence = 16;  // packed-prefill sequence metadata inconsistent
+constexpr int32_t kStatusTimeout = 32;      // a bounded wait gave up (the call's output is void)
+
+// Inter-CTA hand-off through global memory (gpu scope).
+__device__ __forceinline__ int ld_acquire_gpu(const int* ptr) {
+  int v;
+  asm volatile("ld.acquire.gpu.global.b32 %0, [%1];" : "=r"(v) : "l"(ptr) : "memory");
+  return v;
+}
+__device__ __forceinline__ void st_release_gpu(int* ptr, int v) {
+  asm volatile("st.release.gpu.global.b32 [%0], %1;" ::"l"(ptr), "r"(v) : "memory");
+}
 
 __device__ __forceinline__ void raise_status(int32_t* status, int32_t bits) {
   if (status != nullptr) atomicOr(status, bits);

@@ -37,7 +37,7 @@ namespace {
 #define RLT_DECODE_WARPS 4
 #endif
 #ifndef RLT_DECODE_MIN_BLOCKS
-#define RLT_DECODE_MIN_BLOCKS 5
+#define RLT_DECODE_MIN_BLOCKS 4
 #endif
 #ifndef RLT_DECODE_V_EARLY
 #define RLT_DECODE_V_EARLY 1
@@ -45,10 +45,16 @@ namespace {
 #ifndef RLT_DECODE_SPLIT_CHUNK
 #define RLT_DECODE_SPLIT_CHUNK 256
 #endif
+#ifndef RLT_DECODE_TOK_CAP
+#define RLT_DECODE_TOK_CAP 8
+#endif
 constexpr int kDecodeWarps = RLT_DECODE_WARPS;       // warps (= warp tasks) per CTA
 constexpr int kSplitAlign = 32;                      // every split starts at a multiple of this
 constexpr int kSplitChunk = RLT_DECODE_SPLIT_CHUNK;  // target tokens per split
 constexpr int kMaxSplits = 128;                      // cap; longer rows get longer splits
+// Polls (128 ns apart) before a CTA waiting for a split-partial ring slot
+// gives up: about a second, far beyond any real wait.
+constexpr int64_t kRingWaitLimit = int64_t(1) << 23;
 
 struct DecodeParams {
   const void* q;
@@ -60,10 +66,22 @@ struct DecodeParams {
   void* out;
   float* ws_o;   // [rows, launch_splits, hq, head_dim] unnormalised acc
   float* ws_ml;  // [rows, launch_splits, hq, 2] (running max in log2 units, sum)
-  int* counters;  // [rows, hq] finished-split counts (zeroed by the launcher)
-  const int* schedule;  // split launches: [rows + 1] first work item of each row (NULL: one
-                        // item per CTA, blockIdx = (row, head block), split)
+  int* counters;  // [rows, hq] finished-split counts (zeroed by the schedule kernel)
+  const int* schedule;  // split launches: [rows + 1] first work item of each position of
+                        // `order` (NULL: one item per CTA, blockIdx = (row, head block),
+                        // split)
   int* work;            // split launches: next unclaimed work item
+  // Split partials live in a ring of `ring` slots, one slot per (row, split)
+  // of a row that splits: pair j = part_base[row] + split uses slot j % ring
+  // once slot_seq[j % ring] == j, and the row's last merge hands each of its
+  // slots on (slot_seq += ring). Pairs are claimed in row order and a row's
+  // pairs never exceed the ring, so a pair only ever waits for rows whose
+  // work items are all claimed by running CTAs.
+  const int* order;      // [rows]: the rows in scheduling order (most splits first)
+  const int* part_base;  // [rows]: first ring pair of the row (rows with one split: unused)
+  int* row_merges;       // [rows]: head blocks of the row merged so far
+  int* slot_seq;         // [ring]: the pair each slot accepts next
+  int ring;
   float* lse;     // optional [rows, hq]: base-2 log-sum-exp of the scaled scores
                   // (max + log2(sum)); -inf for an empty row. NULL: not written
   int32_t* status;
@@ -103,7 +121,7 @@ __host__ __device__ __forceinline__ int launch_splits_for(int64_t max_ctx) {
 // a token row (so a full reduce-scatter ends with one token per lane), capped
 // so that TOK partials for GC query heads stay in registers.
 __host__ __device__ constexpr int tokens_per_group(int lpt, int gc) {
-  return lpt < 16 / gc ? lpt : 16 / gc;
+  return lpt < RLT_DECODE_TOK_CAP / gc ? lpt : RLT_DECODE_TOK_CAP / gc;
 }
 
 template <int N>
@@ -128,18 +146,24 @@ __device__ __forceinline__ int checked_length(const DecodeParams& p, int row, bo
 // Merge the split partials of one query head of one row (one warp): the
 // splits' base-2 running maxima and sums give each split's weight; the output
 // is the weighted sum of the unnormalised accumulators over the total sum.
+// Partial (acc [head_dim], then (max, sum)) of split `sp` of `row` for query
+// head `qh`: element offset of its ring slot's row.
+__device__ __forceinline__ int64_t partial_row(const DecodeParams& p, int row, int sp, int qh) {
+  const int slot = (p.part_base[row] + sp) % p.ring;
+  return static_cast<int64_t>(slot) * p.hq + qh;
+}
+
 template <typename T>
 __device__ __forceinline__ void merge_splits(const DecodeParams& p, int row, int qh, int count,
                                              int lane) {
-  const int64_t base = static_cast<int64_t>(row) * p.launch_splits * p.hq + qh;
   float mx = -INFINITY;
-  for (int sp = lane; sp < count; sp += 32) mx = fmaxf(mx, p.ws_ml[(base + sp * p.hq) * 2]);
+  for (int sp = lane; sp < count; sp += 32) mx = fmaxf(mx, p.ws_ml[partial_row(p, row, sp, qh) * 2]);
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(kFullMask, mx, o));
   const float mref = mx == -INFINITY ? 0.f : mx;
   float total = 0.f;
   for (int sp = lane; sp < count; sp += 32) {
-    const float2 ml = *reinterpret_cast<const float2*>(p.ws_ml + (base + sp * p.hq) * 2);
+    const float2 ml = *reinterpret_cast<const float2*>(p.ws_ml + partial_row(p, row, sp, qh) * 2);
     total += ml.y * ex2(ml.x - mref);
   }
 #pragma unroll
@@ -151,8 +175,9 @@ __device__ __forceinline__ void merge_splits(const DecodeParams& p, int row, int
   for (int d4 = lane; d4 < p.head_dim / 4; d4 += 32) {
     float4 a = make_float4(0.f, 0.f, 0.f, 0.f);
     for (int sp = 0; sp < count; ++sp) {
-      const float w = ex2(p.ws_ml[(base + sp * p.hq) * 2] - mref);
-      const float4 v = *reinterpret_cast<const float4*>(p.ws_o + (base + sp * p.hq) * p.head_dim + d4 * 4);
+      const int64_t at = partial_row(p, row, sp, qh);
+      const float w = ex2(p.ws_ml[at * 2] - mref);
+      const float4 v = *reinterpret_cast<const float4*>(p.ws_o + at * p.head_dim + d4 * 4);
       a.x = fmaf(v.x, w, a.x);
       a.y = fmaf(v.y, w, a.y);
       a.z = fmaf(v.z, w, a.z);
@@ -436,7 +461,21 @@ __device__ __forceinline__ void decode_item(const DecodeParams& p, const int row
     }
     return;
   }
-  const int64_t slot = (static_cast<int64_t>(row) * p.launch_splits + split) * p.hq + qh0;
+  // The ring slot of this (row, split) must have been handed on by the row
+  // that used it before (bounded wait; on time-out the call is flagged).
+  const int pair = p.part_base[row] + split;
+  if (threadIdx.x == 0) {
+    const int* seq = p.slot_seq + pair % p.ring;
+    for (int64_t spins = 0; ld_acquire_gpu(seq) != pair; ++spins) {
+      if (spins > kRingWaitLimit) {
+        raise_status(p.status, kStatusTimeout);
+        break;
+      }
+      __nanosleep(128);
+    }
+  }
+  __syncthreads();
+  const int64_t slot = static_cast<int64_t>(pair % p.ring) * p.hq + qh0;
   if (active && g == 0) {
 #pragma unroll
     for (int c = 0; c < GC; ++c) {
@@ -462,10 +501,24 @@ __device__ __forceinline__ void decode_item(const DecodeParams& p, const int row
     merge_here = done == plan.count - 1;
   }
   __syncthreads();
-  if (!merge_here || !active) return;
+  if (!merge_here) return;
   __threadfence();
+  if (active) {
 #pragma unroll
-  for (int c = 0; c < GC; ++c) merge_splits<T>(p, row, qh0 + c, plan.count, lane);
+    for (int c = 0; c < GC; ++c) merge_splits<T>(p, row, qh0 + c, plan.count, lane);
+  }
+  // The row's last head block to merge hands its ring slots on.
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    __threadfence();
+    const int tasks_per_row = p.hkv * (p.group / GC);
+    const int blocks_per_row = (tasks_per_row + kDecodeWarps - 1) / kDecodeWarps;
+    if (atomicAdd(p.row_merges + row, 1) == blocks_per_row - 1) {
+      for (int sp = 0; sp < plan.count; ++sp)
+        st_release_gpu(p.slot_seq + (p.part_base[row] + sp) % p.ring,
+                       p.part_base[row] + sp + p.ring);
+    }
+  }
 }
 
 // Split launches run a fixed grid (one resident wave) whose CTAs claim work
@@ -492,47 +545,91 @@ __global__ void __launch_bounds__(kDecodeWarps * 32, RLT_DECODE_MIN_BLOCKS)
     const int item = claimed;
     __syncthreads();  // every thread has read it before thread 0 claims the next
     if (item >= total) break;
-    int lo = 0, hi = p.rows - 1;  // the row: last r with schedule[r] <= item
+    int lo = 0, hi = p.rows - 1;  // the position: last q with schedule[q] <= item
     while (lo < hi) {
       const int mid = (lo + hi + 1) >> 1;
       if (p.schedule[mid] <= item) lo = mid; else hi = mid - 1;
     }
     const int local = item - p.schedule[lo];
-    decode_item<T, D, GC, ALIGNED>(p, lo, local % blocks_per_row, local / blocks_per_row);
+    decode_item<T, D, GC, ALIGNED>(p, p.order[lo], local % blocks_per_row,
+                                   local / blocks_per_row);
   }
 }
 
-// Work items of a split launch: row r gets (its split count, 1 for an empty or
-// invalid row) x head blocks items starting at schedule[r]; schedule[rows] =
-// total. Also clears the merge counters and the claim counter. One CTA.
+// Work items of a split launch. Rows are taken longest first (by split
+// count; the order among rows with equal counts is whatever the placement
+// atomics give, which changes no result: a (row, split) partial and the
+// merge order do not depend on when or where they run), so the longest rows'
+// splits start in the first wave and short rows fill the tail. Position q of
+// that order is row order[q]; it gets (its split count, 1 for an empty or
+// invalid row) x head blocks items starting at schedule[q], schedule[rows] =
+// total, and its splits take ring pairs part_base[order[q]] onwards. Also
+// clears the merge, claim and row-merge counters and the ring. One CTA.
 constexpr int kScheduleThreads = 1024;
+
+__device__ __forceinline__ int scheduled_splits(const DecodeParams& p, int r) {
+  const int len = p.lengths[r];
+  const bool ok = len > 0 && static_cast<int64_t>(len) <= static_cast<int64_t>(p.width) * p.page;
+  return ok ? split_plan(len, p.launch_splits).count : 1;
+}
+
 __global__ void __launch_bounds__(kScheduleThreads) decode_schedule_kernel(
     const __grid_constant__ DecodeParams p, int blocks_per_row, int* counters, int* schedule,
     int* work) {
   __shared__ int scan[kScheduleThreads];
+  __shared__ int pscan[kScheduleThreads];
+  __shared__ int bucket[kMaxSplits + 1];  // rows per split count, then placement cursors
   const int tid = threadIdx.x;
   const int64_t ncounters = static_cast<int64_t>(p.rows) * p.hq;
   for (int64_t i = tid; i < ncounters; i += kScheduleThreads) counters[i] = 0;
+  for (int i = tid; i < p.rows; i += kScheduleThreads) p.row_merges[i] = 0;
+  for (int i = tid; i < p.ring; i += kScheduleThreads) p.slot_seq[i] = i;
+  for (int i = tid; i <= kMaxSplits; i += kScheduleThreads) bucket[i] = 0;
   if (tid == 0) *work = 0;
-  int carry = 0;
+  __syncthreads();
+  for (int r = tid; r < p.rows; r += kScheduleThreads) atomicAdd(&bucket[scheduled_splits(p, r)], 1);
+  __syncthreads();
+  if (tid == 0) {  // first position of each split count, most splits first
+    int at = 0;
+    for (int c = kMaxSplits; c >= 0; --c) {
+      const int n = bucket[c];
+      bucket[c] = at;
+      at += n;
+    }
+  }
+  __syncthreads();
+  int* order = const_cast<int*>(p.order);
+  for (int r = tid; r < p.rows; r += kScheduleThreads)
+    order[atomicAdd(&bucket[scheduled_splits(p, r)], 1)] = r;
+  __syncthreads();  // the order is visible to the whole CTA
+  int carry = 0, pcarry = 0;
+  int* part_base = const_cast<int*>(p.part_base);
   for (int base = 0; base < p.rows; base += kScheduleThreads) {
-    const int r = base + tid;
-    int items = 0;
-    if (r < p.rows) {
-      const int len = p.lengths[r];
-      const bool ok = len > 0 && static_cast<int64_t>(len) <= static_cast<int64_t>(p.width) * p.page;
-      items = (ok ? split_plan(len, p.launch_splits).count : 1) * blocks_per_row;
+    const int q = base + tid;
+    int items = 0, pairs = 0, r = 0;
+    if (q < p.rows) {
+      r = order[q];
+      const int count = scheduled_splits(p, r);
+      items = count * blocks_per_row;
+      pairs = count > 1 ? count : 0;  // rows with one split write no partials
     }
     scan[tid] = items;
+    pscan[tid] = pairs;
     __syncthreads();
-    for (int off = 1; off < kScheduleThreads; off <<= 1) {  // inclusive scan
+    for (int off = 1; off < kScheduleThreads; off <<= 1) {  // inclusive scans
       const int add = tid >= off ? scan[tid - off] : 0;
+      const int padd = tid >= off ? pscan[tid - off] : 0;
       __syncthreads();
       scan[tid] += add;
+      pscan[tid] += padd;
       __syncthreads();
     }
-    if (r < p.rows) schedule[r] = carry + scan[tid] - items;
+    if (q < p.rows) {
+      schedule[q] = carry + scan[tid] - items;
+      part_base[r] = pcarry + pscan[tid] - pairs;
+    }
     carry += scan[kScheduleThreads - 1];
+    pcarry += pscan[kScheduleThreads - 1];
     __syncthreads();
   }
   if (tid == 0) schedule[p.rows] = carry;
@@ -726,17 +823,31 @@ struct DecodeArgs {
 
 size_t align16(size_t n) { return (n + 15) & ~static_cast<size_t>(15); }
 
-// Split scratch: [rows * hq] int merge counters | [rows + 1] schedule | claim
-// counter | acc partials | (max, sum) partials.
-size_t counter_bytes(int rows, int hq) {
-  return align16((static_cast<size_t>(rows) * hq + rows + 2) * sizeof(int));
+// Ring slots of split partials: one per (row, split) the launch can produce
+// when that is few, else enough for the in-flight window -- at least two
+// rows' worth of splits (a row never waits for itself) and kRingMin.
+constexpr int kRingMin = 1024;
+int ring_slots(int rows, int splits) {
+  const int64_t most = static_cast<int64_t>(rows) * splits;
+  const int64_t window = 2 * static_cast<int64_t>(splits) > kRingMin ? 2 * splits : kRingMin;
+  return static_cast<int>(most < window ? most : window);
+}
+
+// Split scratch: [rows * hq] merge counters | [rows + 1] schedule | claim
+// counter | [rows] order | [rows] ring base | [rows] row merges | [ring] slot
+// sequence | acc partials [ring, hq, head_dim] | (max, sum) partials
+// [ring, hq, 2].
+size_t counter_bytes(int rows, int hq, int ring) {
+  return align16((static_cast<size_t>(rows) * hq + 4 * static_cast<size_t>(rows) + 2 + ring) *
+                 sizeof(int));
 }
 
 size_t split_bytes(int rows, int hq, int head_dim, int page, int width) {
   const int splits = launch_splits_for(static_cast<int64_t>(page) * width);
   if (splits <= 1 || rows <= 0 || hq <= 0 || head_dim <= 0) return 0;
-  return counter_bytes(rows, hq) +
-         static_cast<size_t>(rows) * splits * hq * (head_dim + 2) * sizeof(float);
+  const int ring = ring_slots(rows, splits);
+  return counter_bytes(rows, hq, ring) +
+         static_cast<size_t>(ring) * hq * (head_dim + 2) * sizeof(float);
 }
 
 int validate(const DecodeArgs& a) {
@@ -795,12 +906,17 @@ int run(DecodeParams p, int32_t dtype, bool fast, void* split_ws, cudaStream_t s
     // The merge and claim counters and the work schedule are rebuilt on the
     // stream by decode_schedule_kernel on every call (allocation-free and
     // capturable).
-    const size_t cbytes = counter_bytes(p.rows, p.hq);
+    p.ring = ring_slots(p.rows, p.launch_splits);
+    const size_t cbytes = counter_bytes(p.rows, p.hq, p.ring);
     p.counters = static_cast<int*>(split_ws);
     p.schedule = p.counters + static_cast<size_t>(p.rows) * p.hq;
     p.work = const_cast<int*>(p.schedule) + p.rows + 1;
+    p.order = p.work + 1;
+    p.part_base = p.order + p.rows;
+    p.row_merges = const_cast<int*>(p.part_base) + p.rows;
+    p.slot_seq = p.row_merges + p.rows;
     p.ws_o = reinterpret_cast<float*>(static_cast<char*>(split_ws) + cbytes);
-    p.ws_ml = p.ws_o + static_cast<size_t>(p.rows) * p.launch_splits * p.hq * p.head_dim;
+    p.ws_ml = p.ws_o + static_cast<size_t>(p.ring) * p.hq * p.head_dim;
   }
   cudaError_t err;
   switch (dtype) {

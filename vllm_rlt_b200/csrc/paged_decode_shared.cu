@@ -31,6 +31,8 @@ constexpr int kSubTile = 32;   // tokens per shared-memory sub-tile (one per lan
 constexpr int kMaxPairs = 32;  // (member, query head) pairs per CTA
 constexpr int kWarps = 4;
 constexpr int kPairsPerWarp = kMaxPairs / kWarps;
+constexpr int kPhaseChunks = 1;  // the prefix-chunk partials
+constexpr int kPhaseMerge = 2;   // their merge into the suffix result
 
 struct SharedParams {
   const void* q;
@@ -591,14 +593,41 @@ __global__ void __launch_bounds__(kWarps * 32) shared_merge_kernel(
   for (int e = 0; e < kE; ++e) dst[e] = from_f32<T>(acc[e] * inv);
 }
 
+// Per call, from the call's own tables and lengths: row r's suffix table is
+// its table shifted past its prefix_pages[r] shared pages (padded with -1)
+// and its suffix length what its context holds beyond them. A row whose
+// context no longer covers its shared pages is outside the plan: it is
+// flagged and gets an empty suffix.
+__global__ void __launch_bounds__(256) shared_suffix_kernel(
+    const int32_t* __restrict__ tables, const int32_t* __restrict__ lengths,
+    const int32_t* __restrict__ prefix_pages, int32_t* __restrict__ suffix_tables,
+    int32_t* __restrict__ suffix_lengths, int32_t* status, int width, int page, int64_t t_rs) {
+  const int r = blockIdx.x;
+  int skip = prefix_pages[r];
+  const int len = lengths[r];
+  const bool ok = skip >= 0 && skip <= width && len >= 0 &&
+                  static_cast<int64_t>(len) >= static_cast<int64_t>(skip) * page;
+  if (!ok) skip = width;
+  for (int j = threadIdx.x; j < width; j += blockDim.x)
+    suffix_tables[static_cast<int64_t>(r) * width + j] =
+        j + skip < width ? tables[r * t_rs + j + skip] : -1;
+  if (threadIdx.x == 0) {
+    suffix_lengths[r] = ok ? len - skip * page : 0;
+    if (!ok) raise_status(status, kStatusBadLength);
+  }
+}
+
 size_t workspace_bytes(int64_t slots, int hq, int d) {
   return static_cast<size_t>(slots) * hq * (d + 2) * sizeof(float);
 }
 
 template <typename T, int D>
 int launch(const SharedParams& p, int num_chunks, const int32_t* row_slots,
-           const float* suffix_lse, void* out, int64_t o_rs, int64_t o_hs, cudaStream_t stream) {
-  if constexpr (std::is_same<T, float>::value) {
+           const float* suffix_lse, void* out, int64_t o_rs, int64_t o_hs, int phases,
+           cudaStream_t stream) {
+  if (!(phases & kPhaseChunks)) {
+    // merge only
+  } else if constexpr (std::is_same<T, float>::value) {
     constexpr int bytes = SharedLayout<D>::kBytes;
     static cudaError_t attr = cudaFuncSetAttribute(
         shared_range_kernel<T, D>, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
@@ -613,7 +642,7 @@ int launch(const SharedParams& p, int num_chunks, const int32_t* row_slots,
     if (num_chunks > 0)
       shared_range_mma_kernel<T, D><<<dim3(num_chunks, p.hkv), kWarps * 32, bytes, stream>>>(p);
   }
-  if (p.num_rows > 0)
+  if ((phases & kPhaseMerge) && p.num_rows > 0)
     shared_merge_kernel<T, D><<<dim3(p.num_rows, ceil_div(p.hq, kWarps)), kWarps * 32, 0, stream>>>(
         p.ws_o, p.ws_ml, row_slots, suffix_lse, out, p.hq, p.num_slots, o_rs, o_hs);
   return launch_status(cudaGetLastError());
@@ -632,7 +661,22 @@ extern "C" size_t rlt_paged_decode_shared_workspace_bytes(int32_t num_slots, int
   return workspace_bytes(num_slots, num_q_heads, head_dim);
 }
 
-extern "C" int rlt_paged_decode_shared(
+extern "C" int rlt_shared_prefix_suffix(const int32_t* block_tables, const int32_t* context_lengths,
+                                        const int32_t* prefix_pages, int32_t* suffix_tables,
+                                        int32_t* suffix_lengths, int32_t* status,
+                                        int32_t num_rows, int32_t table_width, int32_t page_size,
+                                        int64_t table_row_stride, void* stream) {
+  if (num_rows < 0 || table_width < 0 || page_size <= 0 || table_row_stride < table_width)
+    return RLT_E_SHAPE;
+  if (num_rows == 0) return RLT_OK;
+  shared_suffix_kernel<<<num_rows, 256, 0, static_cast<cudaStream_t>(stream)>>>(
+      block_tables, context_lengths, prefix_pages, suffix_tables, suffix_lengths, status,
+      table_width, page_size, table_row_stride);
+  return launch_status(cudaGetLastError());
+}
+
+namespace {
+int shared_entry(
     const void* q, const void* key_cache, const void* value_cache, const int32_t* block_tables,
     const int32_t* chunks, const int32_t* members, const int32_t* member_slots,
     const int32_t* row_slots, const float* suffix_lse, void* out, void* workspace,
@@ -642,7 +686,8 @@ extern "C" int rlt_paged_decode_shared(
     int32_t num_slots, int32_t num_members, int64_t q_row_stride, int64_t q_head_stride, int64_t k_block_stride,
     int64_t k_token_stride, int64_t k_head_stride, int64_t v_block_stride, int64_t v_token_stride,
     int64_t v_head_stride, int64_t table_row_stride, int64_t out_row_stride,
-    int64_t out_head_stride, float scale, void* stream) {
+    int64_t out_head_stride, float scale, int32_t phases, void* stream) {
+  if (phases < 1 || phases > 3) return RLT_E_SHAPE;
   if (dtype != RLT_F32 && dtype != RLT_F16 && dtype != RLT_BF16) return RLT_E_DTYPE;
   if (head_dim != 64 && head_dim != 128) return RLT_E_HEAD_DIM;
   if (num_q_heads <= 0 || num_kv_heads <= 0 || num_q_heads % num_kv_heads != 0 ||
@@ -654,7 +699,7 @@ extern "C" int rlt_paged_decode_shared(
   if (workspace_size < workspace_bytes(num_slots, num_q_heads, head_dim) ||
       (num_slots > 0 && workspace == nullptr))
     return RLT_E_WORKSPACE;
-  if (suffix_lse == nullptr && num_rows > 0) return RLT_E_SHAPE;
+  if (suffix_lse == nullptr && num_rows > 0 && (phases & kPhaseMerge)) return RLT_E_SHAPE;
   const int elt = dtype == RLT_F32 ? 4 : 2;
   if (!aligned16(key_cache) || !aligned16(value_cache) || !aligned16(workspace) ||
       (k_block_stride * elt) % 16 || (k_token_stride * elt) % 16 || (k_head_stride * elt) % 16 ||
@@ -696,18 +741,46 @@ extern "C" int rlt_paged_decode_shared(
   switch (dtype) {
     case RLT_BF16:
       return d128 ? launch<__nv_bfloat16, 128>(p, num_chunks, row_slots, suffix_lse, out, out_row_stride,
-                                               out_head_stride, s)
+                                               out_head_stride, phases, s)
                   : launch<__nv_bfloat16, 64>(p, num_chunks, row_slots, suffix_lse, out, out_row_stride,
-                                              out_head_stride, s);
+                                              out_head_stride, phases, s);
     case RLT_F16:
       return d128 ? launch<__half, 128>(p, num_chunks, row_slots, suffix_lse, out, out_row_stride,
-                                        out_head_stride, s)
+                                        out_head_stride, phases, s)
                   : launch<__half, 64>(p, num_chunks, row_slots, suffix_lse, out, out_row_stride,
-                                       out_head_stride, s);
+                                       out_head_stride, phases, s);
     default:
       return d128 ? launch<float, 128>(p, num_chunks, row_slots, suffix_lse, out, out_row_stride,
-                                       out_head_stride, s)
+                                       out_head_stride, phases, s)
                   : launch<float, 64>(p, num_chunks, row_slots, suffix_lse, out, out_row_stride,
-                                      out_head_stride, s);
+                                      out_head_stride, phases, s);
   }
+}
+}  // namespace
+
+#define RLT_SHARED_ARGS                                                                       \
+  q, key_cache, value_cache, block_tables, chunks, members, member_slots, row_slots,         \
+      suffix_lse, out, workspace, workspace_size, status, dtype, num_rows, num_q_heads,      \
+      num_kv_heads, head_dim, page_size, table_width, num_blocks, num_chunks, num_slots,     \
+      num_members, q_row_stride, q_head_stride, k_block_stride, k_token_stride,             \
+      k_head_stride, v_block_stride, v_token_stride, v_head_stride, table_row_stride,       \
+      out_row_stride, out_head_stride, scale
+#define RLT_SHARED_PARAMS                                                                     \
+  const void *q, const void *key_cache, const void *value_cache,                             \
+      const int32_t *block_tables, const int32_t *chunks, const int32_t *members,            \
+      const int32_t *member_slots, const int32_t *row_slots, const float *suffix_lse,        \
+      void *out, void *workspace, size_t workspace_size, int32_t *status, int32_t dtype,     \
+      int32_t num_rows, int32_t num_q_heads, int32_t num_kv_heads, int32_t head_dim,         \
+      int32_t page_size, int32_t table_width, int64_t num_blocks, int32_t num_chunks,        \
+      int32_t num_slots, int32_t num_members, int64_t q_row_stride, int64_t q_head_stride,   \
+      int64_t k_block_stride, int64_t k_token_stride, int64_t k_head_stride,                 \
+      int64_t v_block_stride, int64_t v_token_stride, int64_t v_head_stride,                 \
+      int64_t table_row_stride, int64_t out_row_stride, int64_t out_head_stride, float scale
+
+extern "C" int rlt_paged_decode_shared(RLT_SHARED_PARAMS, void* stream) {
+  return shared_entry(RLT_SHARED_ARGS, kPhaseChunks | kPhaseMerge, stream);
+}
+
+extern "C" int rlt_paged_decode_shared_phases(RLT_SHARED_PARAMS, int32_t phases, void* stream) {
+  return shared_entry(RLT_SHARED_ARGS, phases, stream);
 }

@@ -40,7 +40,6 @@ constexpr int kHalfBytes = 128 * 128;     // 128 rows x 64 columns x 2 B
 constexpr int kTileBytes = 2 * kHalfBytes;
 constexpr int kSmemBytes = 6 * kTileBytes + 1024;  // Q, K x2, V x2, P + alignment slack
 constexpr long long kWaitLimit = 100000000LL;      // cycles (~50 ms at 1.9 GHz)
-constexpr int32_t kStatusTimeout = 32;
 constexpr int32_t kStatusLayout = 64;  // dynamic shared memory base too far from 1024-byte alignment
 
 struct PrefillTcParams {
@@ -55,6 +54,9 @@ struct PrefillTcParams {
   int num_seqs, num_tokens, hq, group, page, width;
   int64_t num_blocks, t_rs, o_rs, o_hs;
   float scale_log2;
+  // kSplitP kernels: a query tile whose first row attends fewer keys than
+  // this splits P into hi + lo for every key tile (INT32_MAX: every tile)
+  int split_keys;
 };
 
 // Byte offset of 16-byte chunk c of row r inside one [128 rows x 128 B]
@@ -74,6 +76,21 @@ template <>
 __device__ __forceinline__ uint32_t pack2<__half>(float lo, float hi) {
   __half2 v = __floats2half2_rn(lo, hi);
   return *reinterpret_cast<uint32_t*>(&v);
+}
+
+// The two 16-bit values of a pack2 word, widened exactly to fp32.
+template <typename T>
+__device__ __forceinline__ void unpack2(uint32_t w, float& lo, float& hi);
+template <>
+__device__ __forceinline__ void unpack2<__nv_bfloat16>(uint32_t w, float& lo, float& hi) {
+  lo = __uint_as_float(w << 16);
+  hi = __uint_as_float(w & 0xffff0000u);
+}
+template <>
+__device__ __forceinline__ void unpack2<__half>(uint32_t w, float& lo, float& hi) {
+  const __half2 v = *reinterpret_cast<const __half2*>(&w);
+  lo = __low2float(v);
+  hi = __high2float(v);
 }
 
 
@@ -542,11 +559,23 @@ struct PairLayout {
 static_assert(PairLayout<true>::kSlack >= 0 && PairLayout<false>::kSlack >= 0,
               "shared memory per CTA");
 
-template <typename T, bool kPTmem, int kHalves, bool kWide>
+// kSplitP (wide variant only): in a query tile that splits (its first row
+// attends fewer than p.split_keys keys), P is handed to the PV product as
+// two 16-bit operands, P_hi = round(P) in S_x's first 64 columns and P_lo =
+// round(P - P_hi) in its last 64, and O_x accumulates P_hi V + P_lo V. P
+// then carries about 16 significant bits instead of 8 (bf16), which takes
+// the rounding of P out of the output's error where it matters: a row that
+// attends few keys sees the bf16 rounding of each probability (up to 2^-9
+// relative) almost unaveraged, while over hundreds of keys the independent
+// roundings average out (relative error ~ 2^-9 / sqrt(keys)). The decision is
+// per query tile and made identically by its softmax warps and the MMA
+// thread from the tile's position, so both agree without a hand-off.
+template <typename T, bool kPTmem, int kHalves, bool kWide, bool kSplitP = false>
 __global__ void __launch_bounds__(pair_threads(kHalves, kWide), 1)
     paged_prefill_tc2_kernel(const __grid_constant__ PrefillTcParams p) {
   static_assert(kHalves == 1 || (kHalves == 2 && kPTmem), "split softmax needs P in TMEM");
   static_assert(!kWide || (kHalves == 1 && kPTmem), "wide registers: one warp per row set");
+  static_assert(!kSplitP || kWide, "the split P needs the register-resident scores");
   constexpr int kRingSlots = PairLayout<kPTmem>::kSlots;
   constexpr int kSoftWarps = 8 * kHalves;
   constexpr int kMmaWarp = kSoftWarps;
@@ -741,6 +770,11 @@ __global__ void __launch_bounds__(pair_threads(kHalves, kWide), 1)
         }
       };
       // k-steps [k0, k1) of O_x += P_x V, V in ring slot `slot`
+      [[maybe_unused]] bool split_tile[2] = {false, false};
+      if constexpr (kSplitP) {
+        for (int x = 0; x < 2; ++x)
+          split_tile[x] = ctx - qlen + m0 + x * kTileM + 1 < p.split_keys;
+      }
       auto pv_steps = [&](int x, int slot, int k0, int k1, uint32_t accumulate) {
         const uint32_t vb = v_lo + slot * kTileStep;
 #pragma unroll
@@ -754,6 +788,11 @@ __global__ void __launch_bounds__(pair_threads(kHalves, kWide), 1)
             const uint32_t pcol = ks * 8 + (kHalves == 2 && ks >= 4 ? 32 : 0);
             tc::mma_f16_ts(tmem + 2 * kTileN + x * kHeadDim, tmem + x * kTileN + pcol, bdesc,
                            idesc_pv, acc);
+            if constexpr (kSplitP) {  // the same keys' P_lo, 64 columns further on
+              if (split_tile[x])
+                tc::mma_f16_ts(tmem + 2 * kTileN + x * kHeadDim, tmem + x * kTileN + 64 + pcol,
+                               bdesc, idesc_pv, 1u);
+            }
           } else {
             const uint32_t off = ((ks >> 2) * kHalfBytes + (ks & 3) * 32) >> 4;
             tc::mma_f16_ss(tmem + 2 * kTileN + x * kHeadDim,
@@ -854,6 +893,9 @@ __global__ void __launch_bounds__(pair_threads(kHalves, kWide), 1)
     const uint32_t o_tmem = tmem + 2 * kTileN + x * kHeadDim + h * kOCols + lane_base;
     const int qi = m0 + x * kTileM + r;
     const int row_limit = min(ctx - qlen + qi, ctx - 1);
+    // warp-uniform: the same rule as the MMA thread's
+    [[maybe_unused]] const bool split_tile =
+        kSplitP && ctx - qlen + m0 + x * kTileM + 1 < p.split_keys;
     float m_used = -INFINITY;
     float l_sum = 0.f;
     int t = 0;
@@ -918,27 +960,46 @@ __global__ void __launch_bounds__(pair_threads(kHalves, kWide), 1)
         }
         const uint64_t scale2 = pk2(p.scale_log2, p.scale_log2);
         const uint64_t neg2 = pk2(neg_mref, neg_mref);
-        uint64_t psum2 = pk2(0.f, 0.f);
+        // P of the row's 128 keys into TMEM; with `split`, P_lo beside it.
+        // Two instantiations chosen by one warp-uniform branch, so the common
+        // (unsplit) path carries none of the split's registers.
+        auto emit_p = [&](auto split) {
+          constexpr bool kSplit = decltype(split)::value;
+          uint64_t psum2 = pk2(0.f, 0.f);
 #pragma unroll
-        for (int c = 0; c < 4; ++c) {
-          uint32_t packed[16];
+          for (int c = 0; c < 4; ++c) {
+            uint32_t packed[16];
+            [[maybe_unused]] uint32_t rest[16];  // P_lo
 #pragma unroll
-          for (int j = 0; j < 32; j += 2) {
-            const uint64_t arg =
-                fma2(pk2(__uint_as_float(sr[c][j]), __uint_as_float(sr[c][j + 1])), scale2, neg2);
-            float p0, p1;
-            upk2(arg, p0, p1);
-            if ((j / 2) % 8 < kPolyPairs) {  // this pair on the FMA pipe
-              upk2(exp2_poly2(p0, p1), p0, p1);
-            } else {
-              p0 = ex2(p0);
-              p1 = ex2(p1);
+            for (int j = 0; j < 32; j += 2) {
+              const uint64_t arg = fma2(pk2(__uint_as_float(sr[c][j]), __uint_as_float(sr[c][j + 1])),
+                                        scale2, neg2);
+              float p0, p1;
+              upk2(arg, p0, p1);
+              if ((j / 2) % 8 < kPolyPairs) {  // this pair on the FMA pipe
+                upk2(exp2_poly2(p0, p1), p0, p1);
+              } else {
+                p0 = ex2(p0);
+                p1 = ex2(p1);
+              }
+              psum2 = add2(psum2, pk2(p0, p1));
+              packed[j / 2] = pack2<T>(p0, p1);
+              if constexpr (kSplit) {
+                float h0, h1;
+                unpack2<T>(packed[j / 2], h0, h1);
+                rest[j / 2] = pack2<T>(p0 - h0, p1 - h1);
+              }
             }
-            psum2 = add2(psum2, pk2(p0, p1));
-            packed[j / 2] = pack2<T>(p0, p1);
+            tc::tmem_st16(s_tmem + c * 16, packed);  // S columns already in registers
+            if constexpr (kSplit) tc::tmem_st16(s_tmem + 64 + c * 16, rest);
           }
-          tc::tmem_st16(s_tmem + c * 16, packed);  // S columns already in registers
-        }
+          return psum2;
+        };
+        uint64_t psum2;
+        if (kSplitP && split_tile)
+          psum2 = emit_p(std::integral_constant<bool, kSplitP>{});
+        else
+          psum2 = emit_p(std::false_type{});
         float lo, hi;
         upk2(psum2, lo, hi);
         l_sum = l_sum * factor + (lo + hi);
@@ -1204,27 +1265,30 @@ bool aligned16(const void* ptr) { return (reinterpret_cast<uintptr_t>(ptr) & 15u
 // from TMEM twice, 2 = as 3 with P in shared memory, 1 = the single-tile
 // kernel.
 std::atomic<int> g_prefill_version{5};
+// Version 6 splits P in query tiles whose first row sees fewer keys than
+// this; over more keys the bf16 roundings of P average out (error ~ 2^-9 x
+// 1.6 / sqrt(keys) per output at unit-variance scores, below 1e-4 here).
+constexpr int kSplitKeys = 512;
 
-template <typename T, bool kPTmem, int kHalves, bool kWide = false>
+template <typename T, bool kPTmem, int kHalves, bool kWide = false, bool kSplitP = false>
 cudaError_t launch_pair(dim3 grid, const PrefillTcParams& p, cudaStream_t stream) {
   constexpr int bytes = PairLayout<kPTmem>::kSmemBytes;
+  auto kernel = paged_prefill_tc2_kernel<T, kPTmem, kHalves, kWide, kSplitP>;
   static std::once_flag once;
   static cudaError_t attr_err = cudaSuccess;
-  std::call_once(once, [] {
-    attr_err = cudaFuncSetAttribute(paged_prefill_tc2_kernel<T, kPTmem, kHalves, kWide>,
-                                    cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+  std::call_once(once, [kernel] {
+    attr_err = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
     if (kWide && attr_err == cudaSuccess) {
       // the register split assumes this launch allocation; with fewer
       // registers the softmax warpgroups' increase could never be granted
       cudaFuncAttributes attr{};
-      attr_err = cudaFuncGetAttributes(&attr, paged_prefill_tc2_kernel<T, kPTmem, kHalves, kWide>);
+      attr_err = cudaFuncGetAttributes(&attr, kernel);
       if (attr_err == cudaSuccess && attr.numRegs < kWideLaunchRegs)
         attr_err = cudaErrorInvalidConfiguration;
     }
   });
   if (attr_err != cudaSuccess) return attr_err;
-  paged_prefill_tc2_kernel<T, kPTmem, kHalves, kWide>
-      <<<grid, pair_threads(kHalves, kWide), bytes, stream>>>(p);
+  kernel<<<grid, pair_threads(kHalves, kWide), bytes, stream>>>(p);
   return cudaSuccess;
 }
 
@@ -1295,8 +1359,9 @@ int paged_prefill_tc(const void* q, const void* key_cache, const void* value_cac
   p.o_rs = st[9];
   p.o_hs = st[10];
   p.scale_log2 = scale * 1.4426950408889634f;
-
   const int version = g_prefill_version.load();
+  p.split_keys = version == 7 ? INT32_MAX : kSplitKeys;
+
   if (version == 1) {
     static std::once_flag attr_once[2];
     cudaError_t attr_err = cudaSuccess;
@@ -1326,8 +1391,11 @@ int paged_prefill_tc(const void* q, const void* key_cache, const void* value_cac
   else if (version == 4)
     err = dtype == RLT_BF16 ? launch_pair<__nv_bfloat16, true, 2>(grid, p, stream)
                             : launch_pair<__half, true, 2>(grid, p, stream);
-  else
+  else if (version == 5)
     err = dtype == RLT_BF16 ? launch_pair<__nv_bfloat16, true, 1, true>(grid, p, stream)
+                            : launch_pair<__half, true, 1, true>(grid, p, stream);
+  else  // 6 / 7: bf16 splits P into hi + lo (fp16's 11-bit P needs no split)
+    err = dtype == RLT_BF16 ? launch_pair<__nv_bfloat16, true, 1, true, true>(grid, p, stream)
                             : launch_pair<__half, true, 1, true>(grid, p, stream);
   if (err != cudaSuccess) return static_cast<int>(err);
   return launch_status(cudaGetLastError());
@@ -1337,7 +1405,7 @@ int paged_prefill_tc(const void* q, const void* key_cache, const void* value_cac
 }  // namespace rlt
 
 extern "C" int rlt_prefill_tc_select(int32_t version) {
-  if (version < 1 || version > 5) return rlt::g_prefill_version.load();
+  if (version < 1 || version > 7) return rlt::g_prefill_version.load();
   return rlt::g_prefill_version.exchange(version);
 }
 

@@ -73,6 +73,8 @@ class SharedPrefixPlan:
     row_slots: torch.Tensor     # int32 [N + 1]: row r owns slots row_slots[r]..row_slots[r+1]
     suffix_tables: torch.Tensor   # int32 [N, W]: row's table after its shared pages (-1 padded)
     suffix_lengths: torch.Tensor  # int32 [N]: tokens after the shared prefix
+    prefix_pages: torch.Tensor    # int32 [N]: the row's shared leading pages (0: none)
+    lengths: torch.Tensor         # int32 [N]: the context lengths the plan was built from
     num_rows: int
     num_chunks: int
     num_slots: int
@@ -147,21 +149,42 @@ def plan_shared_prefix(block_tables, context_lengths, page_size: int, num_q_head
     def up(a):
         return torch.from_numpy(np.ascontiguousarray(a)).to(device)
 
+    clipped = np.clip(np.asarray(lengths, dtype=np.int64), 0, None)
+    prefix_pages = ((clipped - suffix_lengths) // page_size).astype(np.int32)
     return SharedPrefixPlan(
         chunks=up(chunks if len(chunks) else np.zeros((0, 5), np.int32)),
         members=up(members), member_slots=up(slots), row_slots=up(row_slots),
         suffix_tables=up(suffix_tables), suffix_lengths=up(suffix_lengths),
+        prefix_pages=up(prefix_pages), lengths=up(clipped.astype(np.int32)),
         num_rows=int(tables.shape[0]), num_chunks=int(len(chunks)), num_slots=int(row_slots[-1]),
         groups=groups, logical_tokens=logical, read_tokens=read)
+
+
+_SIDE_STREAMS = {}
+
+
+def _side_stream(device):
+    index = device.index if device.index is not None else torch.cuda.current_device()
+    stream = _SIDE_STREAMS.get(index)
+    if stream is None:
+        stream = torch.cuda.Stream(device=torch.device("cuda", index))
+        _SIDE_STREAMS[index] = stream
+    return stream
 
 
 def paged_attention_shared(q, key_cache, value_cache, block_tables, plan: SharedPrefixPlan,
                            *, context_lengths=None, out=None):
     """Decode attention over the plan; same inputs and result as
-    ``paged_attention`` (``context_lengths`` is only validated when given:
-    the plan carries the lengths it was built from)."""
-    lengths = context_lengths if context_lengths is not None else torch.zeros(
-        block_tables.shape[0], dtype=torch.int32, device=block_tables.device)
+    ``paged_attention``.
+
+    The plan's groups and chunks stay valid while its rows grow: each call
+    derives the rows' suffix tables and lengths on the device from the call's
+    own ``block_tables`` and ``context_lengths`` (the plan's lengths when
+    none are given), so a captured CUDA graph can replay the call step after
+    step. Rebuild the plan when the batch's rows change. The prefix chunks
+    run on a second stream while the plain decode kernel computes the
+    suffixes; the merge joins them on the caller's stream."""
+    lengths = _as_int32(context_lengths) if context_lengths is not None else plan.lengths
     _validate(q, key_cache, value_cache, block_tables, lengths)
     if q.shape[-1] not in (64, 128):
         raise ValueError("the shared-prefix decode supports head_dim 64 or 128")
@@ -179,36 +202,61 @@ def paged_attention_shared(q, key_cache, value_cache, block_tables, plan: Shared
     status = _lib.status_word(device).data_ptr()
     stream = _lib.stream_of(device)
     scale = d ** -0.5
-    # 1. each row's own tokens after its shared prefix: the plain decode kernel
-    suffix = plan.suffix_tables
+    tables = _as_int32(block_tables)
+    width = tables.shape[1]
+    # 0. this call's suffix tables and lengths
+    suffix = torch.empty((rows, width), dtype=torch.int32, device=device)
+    suffix_lengths = torch.empty(rows, dtype=torch.int32, device=device)
+    code = lib.rlt_shared_prefix_suffix(
+        tables.data_ptr(), lengths.data_ptr(), plan.prefix_pages.data_ptr(), suffix.data_ptr(),
+        suffix_lengths.data_ptr(), status, rows, width, page, tables.stride(0), stream)
+    _lib.check(code, "shared-prefix suffix metadata")
+    dtype_code = _lib.DTYPE_CODES[q.dtype]
+
+    def shared(phases, launch_stream, workspace, lse):
+        return lib.rlt_paged_decode_shared_phases(
+            q.data_ptr(), key_cache.data_ptr(), value_cache.data_ptr(), tables.data_ptr(),
+            plan.chunks.data_ptr(), plan.members.data_ptr(), plan.member_slots.data_ptr(),
+            plan.row_slots.data_ptr(), _lib.ptr(lse), output.data_ptr(), workspace.data_ptr(),
+            workspace.numel(), status, dtype_code,
+            rows, hq, hkv, d, page, width, key_cache.shape[0],
+            plan.num_chunks, plan.num_slots, plan.members.numel(),
+            q.stride(0), q.stride(1),
+            key_cache.stride(0), key_cache.stride(1), key_cache.stride(2),
+            value_cache.stride(0), value_cache.stride(1), value_cache.stride(2),
+            tables.stride(0), output.stride(0), output.stride(1), scale, phases, launch_stream)
+
+    # 1. the shared prefixes, read once per group, on the side stream
+    need = lib.rlt_paged_decode_shared_workspace_bytes(plan.num_slots, hq, d)
+    workspace = torch.empty(max(need, 16), dtype=torch.uint8, device=device)
+    overlap = plan.num_chunks > 0
+    if overlap:
+        current = torch.cuda.current_stream(device)
+        side = _side_stream(device)
+        fork = torch.cuda.Event()
+        fork.record(current)
+        side.wait_event(fork)
+        _lib.check(shared(1, side.cuda_stream, workspace, None),
+                   "shared-prefix paged decode attention (prefix chunks)")
+        workspace.record_stream(side)
+    # 2. each row's own tokens after its shared prefix: the plain decode kernel
     lse = torch.empty((rows, hq), dtype=torch.float32, device=device)
-    need = lib.rlt_paged_decode_workspace_bytes(rows, hq, d, page, suffix.shape[1])
+    need = lib.rlt_paged_decode_workspace_bytes(rows, hq, d, page, width)
     decode_ws = torch.empty(need, dtype=torch.uint8, device=device) if need else None
     code = lib.rlt_paged_decode_lse(
         q.data_ptr(), key_cache.data_ptr(), value_cache.data_ptr(), suffix.data_ptr(),
-        plan.suffix_lengths.data_ptr(), output.data_ptr(), _lib.ptr(decode_ws), need, status,
-        _lib.DTYPE_CODES[q.dtype], rows, hq, hkv, d, page, suffix.shape[1], key_cache.shape[0],
+        suffix_lengths.data_ptr(), output.data_ptr(), _lib.ptr(decode_ws), need, status,
+        dtype_code, rows, hq, hkv, d, page, width, key_cache.shape[0],
         q.stride(0), q.stride(1),
         key_cache.stride(0), key_cache.stride(1), key_cache.stride(2),
         value_cache.stride(0), value_cache.stride(1), value_cache.stride(2),
         suffix.stride(0), output.stride(0), output.stride(1), scale, lse.data_ptr(), stream,
     )
     _lib.check(code, "shared-prefix paged decode attention (suffixes)")
-    # 2. the shared prefixes, read once per group, merged into the output
-    tables = _as_int32(block_tables)
-    need = lib.rlt_paged_decode_shared_workspace_bytes(plan.num_slots, hq, d)
-    workspace = torch.empty(max(need, 16), dtype=torch.uint8, device=device)
-    code = lib.rlt_paged_decode_shared(
-        q.data_ptr(), key_cache.data_ptr(), value_cache.data_ptr(), tables.data_ptr(),
-        plan.chunks.data_ptr(), plan.members.data_ptr(), plan.member_slots.data_ptr(),
-        plan.row_slots.data_ptr(), lse.data_ptr(), output.data_ptr(), workspace.data_ptr(),
-        workspace.numel(), status, _lib.DTYPE_CODES[q.dtype],
-        rows, hq, hkv, d, page, tables.shape[1], key_cache.shape[0],
-        plan.num_chunks, plan.num_slots, plan.members.numel(),
-        q.stride(0), q.stride(1),
-        key_cache.stride(0), key_cache.stride(1), key_cache.stride(2),
-        value_cache.stride(0), value_cache.stride(1), value_cache.stride(2),
-        tables.stride(0), output.stride(0), output.stride(1), scale, stream,
-    )
-    _lib.check(code, "shared-prefix paged decode attention")
+    # 3. the merge, once both are done
+    if overlap:
+        join = torch.cuda.Event()
+        join.record(side)
+        current.wait_event(join)
+        _lib.check(shared(2, stream, workspace, lse), "shared-prefix paged decode attention (merge)")
     return output
