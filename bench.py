@@ -64,7 +64,8 @@ def parse():
     p.add_argument("--no-extras", action="store_true",
                    help="skip the Ouro, prefill, long-context and shared-prefix sub-measurements")
     p.add_argument("--workload",
-                   choices=["decode", "prefill", "longctx", "ouro", "shared", "kernels"],
+                   choices=["decode", "prefill", "longctx", "ouro", "shared", "kernels",
+                            "reference-engine"],
                    default="decode",
                    help="decode: the headline line; the others: that workload alone")
     return p.parse_args()
@@ -149,6 +150,22 @@ class ClockSampler:
 
 
 # --------------------------------------------------------- reference (CPU)
+
+
+def decode_config(plan, world):
+    """The headline workload's config, shared by both arms' lines."""
+    from vllm_rlt_b200.kernels.paged_attention import decode_bytes
+
+    return {
+        "workload": WORKLOAD,
+        "rows_per_gpu": plan.num_rows,
+        "sum_ctx_per_gpu": int(plan.context_lengths.sum()),
+        "bytes_per_step_per_gpu": int(decode_bytes(plan.context_lengths, plan.num_q_heads,
+                                                   plan.num_kv_heads, plan.head_dim, 2,
+                                                   plan.page)),
+        "l2": "no flush: each step reads ~5 GB of K/V (> 126 MB L2)",
+        "parallelism": f"{world} request-sharded replicas, no data-path collective",
+    }
 
 
 def reference_module(name):
@@ -291,6 +308,50 @@ def reference_kv_cpu(batch=64, reps=20):
             "threads": torch.get_num_threads(), "kind": "reference"}
 
 
+def reference_engine_cpu(requests=4, prompt=16, new_tokens=8):
+    """BASELINE B5: the reference's own engine end to end on the host cores --
+    LLMEngine with its torch attention backend (vllm_rlt/engine/llm_engine.py,
+    vllm_rlt/kernels/paged_attention.py:12-36) serving a random-init
+    Ouro-1.4B-shaped model (24 layers x 4 loops, 2048 hidden, 16x128 heads,
+    SwiGLU 5632, vocab 49152, RoPE 1e4) in fp32, a reduced batch, exit depth
+    per token from a seeded trace in {1..4}. Plumbing only: no GPU."""
+    import torch
+
+    config_mod = reference_module("vllm_rlt.models")
+    engine_mod = reference_module("vllm_rlt.engine.llm_engine")
+    root = reference_module("vllm_rlt")
+    if config_mod is None or engine_mod is None or root is None:
+        return {"unavailable": "the reference is not installed under baseline/_ref"}
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    torch.manual_seed(0)
+    t0 = time.perf_counter()
+    model = config_mod.OuroForCausalLM(config_mod.OuroConfig(rope_theta=10000.0)).eval()
+    build_s = time.perf_counter() - t0
+    rng = np.random.default_rng(8)
+    # the first output follows the prompt's prefill (all 4 loops); later ones exit at 1..4
+    traces = {str(i): [4] + [int(x) for x in rng.integers(1, 5, size=new_tokens + 3)]
+              for i in range(requests)}
+    engine = engine_mod.LLMEngine(
+        model, cache_config=root.CacheConfig(num_blocks=requests * 8, block_size=16),
+        exit_config=root.ExitConfig("trace", depths_by_request=traces),
+        attention_backend="torch")
+    for i in range(requests):
+        engine.add_request(str(i), [int(x) for x in rng.integers(0, 49152, size=prompt)],
+                           root.SamplingParams(max_tokens=new_tokens, ignore_eos=True))
+    t0 = time.perf_counter()
+    generated = 0
+    while engine.has_unfinished_requests():
+        for out in engine.step():
+            if out.finished:
+                generated += len(out.token_ids)
+    run_s = time.perf_counter() - t0
+    return {"tok_s": round(generated / run_s, 3), "tokens": generated, "seconds": round(run_s, 2),
+            "model_init_s": round(build_s, 1), "threads": threads,
+            "batch": f"{requests} requests x {prompt}-token prompts, {new_tokens} new tokens each",
+            "kind": "reference", "dtype": "fp32 (the reference's CPU default)"}
+
+
 def run_reference(args):
     from vllm_rlt_b200 import workloads
 
@@ -317,8 +378,10 @@ def run_reference(args):
         "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": round(total / args.steps * 1e3, 3), "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
-        "config": {"workload": WORKLOAD, "sample": sample, "l2": "host run",
-                   "same_config": len(host.rows) == plan.num_rows},
+        "config": (decode_config(plan, 1) if len(host.rows) == plan.num_rows else
+                   {"workload": WORKLOAD, "rows_per_gpu": len(host.rows),
+                    "sum_ctx_per_gpu": host.tokens, "bytes_per_step_per_gpu": int(host.bytes),
+                    "sample": sample}),
         "cpu_baseline": {"value": round(value, 3), "unit": "GB/s", "cores": threads,
                          "kind": kind, "sample": sample},
         "e2e": {"value": round(value, 3), "unit": "GB/s", "h2d_bytes_per_step": 0,
@@ -1092,14 +1155,7 @@ def run_ours(args):
         "dtype": "bf16",
         "data": "synthetic",
         "pct_of_peak": round(100.0 * value / world / peak, 2),
-        "config": {
-            "workload": WORKLOAD,
-            "rows_per_gpu": plan.num_rows,
-            "sum_ctx_per_gpu": int(plan.context_lengths.sum()),
-            "bytes_per_step_per_gpu": int(step_bytes),
-            "l2": "no flush: each step reads ~5 GB of K/V (> 126 MB L2)",
-            "parallelism": f"{world} request-sharded replicas, no data-path collective",
-        },
+        "config": decode_config(plan, world),
         "roofline": {
             "bound": "hbm",
             "achieved": round(achieved, 1),
@@ -1135,6 +1191,10 @@ def run_ours(args):
 
 def main():
     args = parse()
+    if args.workload == "reference-engine":  # host only
+        print(json.dumps({"workload_line": "reference-engine", **reference_engine_cpu()}),
+              flush=True)
+        return
     if args.impl == "reference":
         run_reference(args)
     elif args.impl == "reference-triton":

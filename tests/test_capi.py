@@ -46,19 +46,20 @@ def test_host_only_entry_points_without_gpu():
     assert lib.rlt_paged_decode_workspace_bytes(8, 16, 128, 16, 16) == 0
     # The reference's graph width 4096 x page 16 allows 128 splits per row;
     # split partials (fp32 acc + max + sum per query head) live in a ring of
-    # max(2 x 128, 1024) (row, split) slots, not rows x 128. Before them the
+    # max(2 x 128, 4096) (row, split) slots, not rows x 128. Before them the
     # int metadata: one merge counter per (row, query head), the rows + 1
     # work schedule, the claim counter, the row order, each row's first ring
-    # pair, per-row merge counts and one sequence word per ring slot,
-    # rounded to 16 bytes.
+    # pair, per-row merge counts, one sequence word per ring slot and the
+    # wrap flag, rounded to 16 bytes.
     def expected(rows, ring):
-        meta = (rows * 16 + 4 * rows + 2 + ring) * 4
+        meta = (rows * 16 + 4 * rows + 3 + ring) * 4
         return (meta + 15) // 16 * 16 + ring * 16 * 130 * 4
 
-    assert lib.rlt_paged_decode_workspace_bytes(256, 16, 128, 16, 4096) == expected(256, 1024)
-    assert lib.rlt_paged_decode_workspace_bytes(256, 16, 128, 16, 4096) < 9 << 20
+    assert lib.rlt_paged_decode_workspace_bytes(256, 16, 128, 16, 4096) == expected(256, 4096)
+    assert lib.rlt_paged_decode_workspace_bytes(256, 16, 128, 16, 4096) < 35 << 20
     # few rows: one slot per possible (row, split), no ring wrap-around
     assert lib.rlt_paged_decode_workspace_bytes(4, 16, 128, 16, 4096) == expected(4, 4 * 128)
+    assert lib.rlt_paged_decode_workspace_bytes(40, 16, 128, 16, 4096) == expected(40, 4096)
     assert lib.rlt_paged_prefill_workspace_bytes(0, 16, 128, 16, 64) == 0
 
 

@@ -177,3 +177,45 @@ def test_prefill_batch_invariance_bit_identical_sequences(dtype, d, group):
     for rows in ([2, 3], [3, 0], [1], [2]):
         for r, part in zip(rows, run(rows)):
             assert torch.equal(part, together[r]), (rows, r)
+
+
+@pytest.mark.parametrize("dtype", ["bf16", "f16"])
+@pytest.mark.parametrize("version", [1, 5, 6])
+def test_pool_garbage_past_the_context_never_reaches_the_output(dtype, version):
+    """Pages are copied whole, so the last context page's slots past the
+    context come along; a pool allocated without initialisation may hold NaN
+    there (the reference's KVCacheManager allocates its pools with
+    torch.empty). Every slot the context does not cover is NaN here; the
+    output must equal the oracle, which reads only the context."""
+    rng = np.random.default_rng(17)
+    page, hkv, d = 16, 2, 128
+    prefix, chunk = [0, 37, 5], [23, 91, 140]
+    lengths = [s + c for s, c in zip(prefix, chunk)]
+    width = max(math.ceil(n / page) for n in lengths)
+    num_blocks = sum(math.ceil(n / page) for n in lengths) + 2
+    perm = rng.permutation(num_blocks)
+    tables = np.full((3, width), -1, dtype=np.int32)
+    c = 0
+    for i, n in enumerate(lengths):
+        tables[i, : math.ceil(n / page)] = perm[c : c + math.ceil(n / page)]
+        c += math.ceil(n / page)
+    td = TORCH[dtype]
+    g = torch.Generator(device="cuda").manual_seed(3)
+    key = torch.full((num_blocks, page, hkv, d), float("nan"), device="cuda", dtype=td)
+    value = torch.full_like(key, float("nan"))
+    for i, n in enumerate(lengths):
+        pos = torch.arange(n, device="cuda")
+        blocks = torch.from_numpy(tables[i]).cuda().long()[pos // page]
+        key[blocks, pos % page] = torch.randn(n, hkv, d, generator=g, device="cuda").to(td)
+        value[blocks, pos % page] = torch.randn(n, hkv, d, generator=g, device="cuda").to(td)
+    cu = np.concatenate([[0], np.cumsum(chunk)]).astype(np.int32)
+    q = torch.randn(int(cu[-1]), hkv, d, generator=g, device="cuda").to(td)
+    out = _with_version(version, lambda: rb.paged_prefill(
+        q, key, value, torch.from_numpy(tables).cuda(),
+        torch.tensor(lengths, dtype=torch.int32, device="cuda"), torch.from_numpy(cu).cuda(),
+        max(chunk)))
+    assert torch.isfinite(out).all()
+    expected = oracle.paged_prefill(to_numpy(q), to_numpy(key), to_numpy(value), tables,
+                                    np.array(lengths), cu, dtype)
+    tol = FA4_TOLERANCE[dtype] if version in ROUNDED_P_VERSIONS else {}
+    assert_close(to_numpy(out), expected, dtype, **tol)

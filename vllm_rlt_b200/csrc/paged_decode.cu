@@ -48,6 +48,9 @@ namespace {
 #ifndef RLT_DECODE_TOK_CAP
 #define RLT_DECODE_TOK_CAP 8
 #endif
+#ifndef RLT_DECODE_LPT
+#define RLT_DECODE_LPT 1
+#endif
 constexpr int kDecodeWarps = RLT_DECODE_WARPS;       // warps (= warp tasks) per CTA
 constexpr int kSplitAlign = 32;                      // every split starts at a multiple of this
 constexpr int kSplitChunk = RLT_DECODE_SPLIT_CHUNK;  // target tokens per split
@@ -81,6 +84,7 @@ struct DecodeParams {
   const int* part_base;  // [rows]: first ring pair of the row (rows with one split: unused)
   int* row_merges;       // [rows]: head blocks of the row merged so far
   int* slot_seq;         // [ring]: the pair each slot accepts next
+  int* ring_wraps;       // set by the schedule: this call's pairs exceed the ring
   int ring;
   float* lse;     // optional [rows, hq]: base-2 log-sum-exp of the scaled scores
                   // (max + log2(sum)); -inf for an empty row. NULL: not written
@@ -464,17 +468,20 @@ __device__ __forceinline__ void decode_item(const DecodeParams& p, const int row
   // The ring slot of this (row, split) must have been handed on by the row
   // that used it before (bounded wait; on time-out the call is flagged).
   const int pair = p.part_base[row] + split;
-  if (threadIdx.x == 0) {
-    const int* seq = p.slot_seq + pair % p.ring;
-    for (int64_t spins = 0; ld_acquire_gpu(seq) != pair; ++spins) {
-      if (spins > kRingWaitLimit) {
-        raise_status(p.status, kStatusTimeout);
-        break;
+  const bool wraps = *p.ring_wraps != 0;  // uniform over the launch
+  if (wraps) {
+    if (threadIdx.x == 0) {
+      const int* seq = p.slot_seq + pair % p.ring;
+      for (int64_t spins = 0; ld_acquire_gpu(seq) != pair; ++spins) {
+        if (spins > kRingWaitLimit) {
+          raise_status(p.status, kStatusTimeout);
+          break;
+        }
+        __nanosleep(128);
       }
-      __nanosleep(128);
     }
+    __syncthreads();
   }
-  __syncthreads();
   const int64_t slot = static_cast<int64_t>(pair % p.ring) * p.hq + qh0;
   if (active && g == 0) {
 #pragma unroll
@@ -507,7 +514,9 @@ __device__ __forceinline__ void decode_item(const DecodeParams& p, const int row
 #pragma unroll
     for (int c = 0; c < GC; ++c) merge_splits<T>(p, row, qh0 + c, plan.count, lane);
   }
-  // The row's last head block to merge hands its ring slots on.
+  // The row's last head block to merge hands its ring slots on (only when
+  // this call's pairs wrap around the ring; otherwise no slot is reused).
+  if (!wraps) return;
   __syncthreads();
   if (threadIdx.x == 0) {
     __threadfence();
@@ -600,7 +609,7 @@ __global__ void __launch_bounds__(kScheduleThreads) decode_schedule_kernel(
   __syncthreads();
   int* order = const_cast<int*>(p.order);
   for (int r = tid; r < p.rows; r += kScheduleThreads)
-    order[atomicAdd(&bucket[scheduled_splits(p, r)], 1)] = r;
+    order[RLT_DECODE_LPT ? atomicAdd(&bucket[scheduled_splits(p, r)], 1) : r] = r;
   __syncthreads();  // the order is visible to the whole CTA
   int carry = 0, pcarry = 0;
   int* part_base = const_cast<int*>(p.part_base);
@@ -632,7 +641,10 @@ __global__ void __launch_bounds__(kScheduleThreads) decode_schedule_kernel(
     pcarry += pscan[kScheduleThreads - 1];
     __syncthreads();
   }
-  if (tid == 0) schedule[p.rows] = carry;
+  if (tid == 0) {
+    schedule[p.rows] = carry;
+    *p.ring_wraps = pcarry > p.ring;
+  }
 }
 
 // Any head_dim <= 256, any alignment: one warp per (row, query head), dims
@@ -826,7 +838,7 @@ size_t align16(size_t n) { return (n + 15) & ~static_cast<size_t>(15); }
 // Ring slots of split partials: one per (row, split) the launch can produce
 // when that is few, else enough for the in-flight window -- at least two
 // rows' worth of splits (a row never waits for itself) and kRingMin.
-constexpr int kRingMin = 1024;
+constexpr int kRingMin = 4096;
 int ring_slots(int rows, int splits) {
   const int64_t most = static_cast<int64_t>(rows) * splits;
   const int64_t window = 2 * static_cast<int64_t>(splits) > kRingMin ? 2 * splits : kRingMin;
@@ -835,10 +847,10 @@ int ring_slots(int rows, int splits) {
 
 // Split scratch: [rows * hq] merge counters | [rows + 1] schedule | claim
 // counter | [rows] order | [rows] ring base | [rows] row merges | [ring] slot
-// sequence | acc partials [ring, hq, head_dim] | (max, sum) partials
-// [ring, hq, 2].
+// sequence | ring wrap flag | acc partials [ring, hq, head_dim] | (max, sum)
+// partials [ring, hq, 2].
 size_t counter_bytes(int rows, int hq, int ring) {
-  return align16((static_cast<size_t>(rows) * hq + 4 * static_cast<size_t>(rows) + 2 + ring) *
+  return align16((static_cast<size_t>(rows) * hq + 4 * static_cast<size_t>(rows) + 3 + ring) *
                  sizeof(int));
 }
 
@@ -915,6 +927,7 @@ int run(DecodeParams p, int32_t dtype, bool fast, void* split_ws, cudaStream_t s
     p.part_base = p.order + p.rows;
     p.row_merges = const_cast<int*>(p.part_base) + p.rows;
     p.slot_seq = p.row_merges + p.rows;
+    p.ring_wraps = p.slot_seq + p.ring;
     p.ws_o = reinterpret_cast<float*>(static_cast<char*>(split_ws) + cbytes);
     p.ws_ml = p.ws_o + static_cast<size_t>(p.ring) * p.hq * p.head_dim;
   }

@@ -78,6 +78,28 @@ __device__ __forceinline__ uint32_t pack2<__half>(float lo, float hi) {
   return *reinterpret_cast<uint32_t*>(&v);
 }
 
+// Key rows past the context in the last key tile. The tile is copied a whole
+// page at a time, so the rows of the last context page beyond the context
+// hold whatever the pool held there -- possibly NaN or Inf bit patterns in a
+// pool allocated without initialisation. Their scores are masked (P = 0),
+// but 0 x NaN is NaN in the PV product, so their V rows must be zeros. Rows
+// of pages wholly past the context were zero-filled by the copy already.
+// Called by one thread once the tile has landed; the caller then fences the
+// generic writes against the tensor core's async-proxy reads.
+__device__ __forceinline__ void zero_tail_rows(uint8_t* v_tile, int ctx, int tile_start, int page) {
+  const int r0 = ctx - tile_start;
+  const int page_end = (ctx + page - 1) / page * page;
+  const int r1 = min(kTileN, page_end - tile_start);
+  if (r0 < 0 || r0 >= r1) return;
+  const uint4 zero = make_uint4(0, 0, 0, 0);
+  for (int r = r0; r < r1; ++r)  // a row is 128 contiguous bytes of each 64-column half
+#pragma unroll
+    for (int half = 0; half < 2; ++half)
+#pragma unroll
+      for (int c = 0; c < 8; ++c)
+        *reinterpret_cast<uint4*>(v_tile + half * kHalfBytes + r * 128 + c * 16) = zero;
+}
+
 // The two 16-bit values of a pack2 word, widened exactly to fp32.
 template <typename T>
 __device__ __forceinline__ void unpack2(uint32_t w, float& lo, float& hi);
@@ -311,6 +333,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (tid == 0 && !abort_flag) {
         if (tc::mbar_wait(&bar_kv[st], (t >> 1) & 1, kWaitLimit)) {
           tc::tc_fence_after();
+          if (t == n_tiles - 1) {
+            zero_tail_rows(sV[st], ctx, t * kTileN, p.page);
+            tc::fence_proxy_async_smem();
+          }
 #pragma unroll
           for (int ks = 0; ks < kHeadDim / 16; ++ks) {
             const uint32_t off = (ks >> 2) * kHalfBytes + (ks & 3) * 32;
@@ -570,9 +596,8 @@ static_assert(PairLayout<true>::kSlack >= 0 && PairLayout<false>::kSlack >= 0,
 // roundings average out (relative error ~ 2^-9 / sqrt(keys)). The decision is
 // per query tile and made identically by its softmax warps and the MMA
 // thread from the tile's position, so both agree without a hand-off.
-template <typename T, bool kPTmem, int kHalves, bool kWide, bool kSplitP = false>
-__global__ void __launch_bounds__(pair_threads(kHalves, kWide), 1)
-    paged_prefill_tc2_kernel(const __grid_constant__ PrefillTcParams p) {
+template <typename T, bool kPTmem, int kHalves, bool kWide, bool kSplitP>
+__device__ __forceinline__ void pair_body(const PrefillTcParams& p) {
   static_assert(kHalves == 1 || (kHalves == 2 && kPTmem), "split softmax needs P in TMEM");
   static_assert(!kWide || (kHalves == 1 && kPTmem), "wide registers: one warp per row set");
   static_assert(!kSplitP || kWide, "the split P needs the register-resident scores");
@@ -788,15 +813,19 @@ __global__ void __launch_bounds__(pair_threads(kHalves, kWide), 1)
             const uint32_t pcol = ks * 8 + (kHalves == 2 && ks >= 4 ? 32 : 0);
             tc::mma_f16_ts(tmem + 2 * kTileN + x * kHeadDim, tmem + x * kTileN + pcol, bdesc,
                            idesc_pv, acc);
-            if constexpr (kSplitP) {  // the same keys' P_lo, 64 columns further on
-              if (split_tile[x])
-                tc::mma_f16_ts(tmem + 2 * kTileN + x * kHeadDim, tmem + x * kTileN + 64 + pcol,
-                               bdesc, idesc_pv, 1u);
-            }
           } else {
             const uint32_t off = ((ks >> 2) * kHalfBytes + (ks & 3) * 32) >> 4;
             tc::mma_f16_ss(tmem + 2 * kTileN + x * kHeadDim,
                            tc::desc64(q_lo + (2 + x) * kTileStep + off, q_hi), bdesc, idesc_pv, acc);
+          }
+        }
+        if constexpr (kSplitP) {
+          // the same keys' P_lo, 64 columns further on: one branch per tile
+          if (split_tile[x]) {
+#pragma unroll
+            for (int ks = k0; ks < k1; ++ks)
+              tc::mma_f16_ts(tmem + 2 * kTileN + x * kHeadDim, tmem + x * kTileN + 64 + ks * 8,
+                             tc::desc64(vb + ks * (2048 >> 4), v_hi), idesc_pv, 1u);
           }
         }
       };
@@ -857,8 +886,12 @@ __global__ void __launch_bounds__(pair_threads(kHalves, kWide), 1)
         // the softmax of tile A still runs keeps them off the path from P_A
         // to the MMAs. The P barriers are polled (test_wait, never
         // suspended): this one thread's wake-up is on the critical path.
-        ok = wait_item(2 * t + 1) && (!more || wait_item(2 * t + 2)) &&
-             tc::mbar_poll(&bar_p[0], t & 1, kWaitLimit);
+        ok = wait_item(2 * t + 1) && (!more || wait_item(2 * t + 2));
+        if (ok && !more) {
+          zero_tail_rows(ring + v_slot * kTileBytes, ctx, t * kTileN, p.page);
+          tc::fence_proxy_async_smem();
+        }
+        ok = ok && tc::mbar_poll(&bar_p[0], t & 1, kWaitLimit);
         if (!ok) break;
         tc::tc_fence_after();
         after_p(0, v_slot, k_next, more, accumulate);
@@ -1228,6 +1261,55 @@ __global__ void __launch_bounds__(pair_threads(kHalves, kWide), 1)
     tc::tc_fence_after();
     tc::tmem_dealloc(tmem, kPairTmemCols);
   }
+}
+
+// The kernel: CTAs whose query tile A sees fewer than p.split_keys keys (tile
+// B sees more) run the body that can split P; all others run the body
+// compiled without it, so the common path carries none of the split's
+// registers or branches. Every warp finds its CTA's tile by itself (warp
+// shuffles only), so the choice needs no shared memory and no barrier.
+template <typename T, bool kPTmem, int kHalves, bool kWide, bool kSplitP = false>
+__global__ void __launch_bounds__(pair_threads(kHalves, kWide), 1)
+    paged_prefill_tc2_kernel(const __grid_constant__ PrefillTcParams p) {
+  if constexpr (kSplitP) {
+    const int lane = threadIdx.x & 31;
+    int running = 0, seq = -1, m0 = 0;
+    for (int base = 0; base < p.num_seqs && seq < 0; base += 32) {  // as find_tile
+      const int sq = base + lane;
+      int tiles = 0;
+      if (sq < p.num_seqs) {
+        const int qlen = p.cu[sq + 1] - p.cu[sq];
+        tiles = qlen > 0 ? (qlen + kPairRows - 1) / kPairRows : 0;
+      }
+      int incl = tiles;
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const int y = __shfl_up_sync(kFullMask, incl, o);
+        if (lane >= o) incl += y;
+      }
+      const int excl = running + incl - tiles;
+      const int target = static_cast<int>(blockIdx.x);
+      const bool mine = sq < p.num_seqs && target >= excl && target < excl + tiles;
+      const unsigned hit = __ballot_sync(kFullMask, mine);
+      if (hit) {
+        const int src = __ffs(hit) - 1;
+        seq = __shfl_sync(kFullMask, sq, src);
+        const int idx = __shfl_sync(kFullMask, tiles - 1 - (target - excl), src);  // heavy first
+        m0 = idx * kPairRows;
+      }
+      running += __shfl_sync(kFullMask, incl, 31);
+    }
+    bool split = false;
+    if (seq >= 0) {
+      const int qlen = p.cu[seq + 1] - p.cu[seq];
+      split = p.lengths[seq] - qlen + m0 + 1 < p.split_keys;
+    }
+    if (split) {
+      pair_body<T, kPTmem, kHalves, kWide, true>(p);
+      return;
+    }
+  }
+  pair_body<T, kPTmem, kHalves, kWide, false>(p);
 }
 
 // ---- host side --------------------------------------------------------------
