@@ -1341,12 +1341,15 @@ bool encode(CUtensorMap* map, CUtensorMapDataType type, uint32_t rank, const voi
 
 bool aligned16(const void* ptr) { return (reinterpret_cast<uintptr_t>(ptr) & 15u) == 0; }
 
-// Which tensor-core kernel rlt_paged_prefill launches: 5 = warp-specialised
-// two-tile kernel with P in TMEM and register-resident scores (default), 4 =
-// split softmax (two warps per row set), 3 = one warp per row set reading S
-// from TMEM twice, 2 = as 3 with P in shared memory, 1 = the single-tile
-// kernel.
-std::atomic<int> g_prefill_version{5};
+// Which tensor-core kernel rlt_paged_prefill launches: 6 (default) = 5 with
+// bf16 P split into hi + lo in the query tiles that attend few keys, 7 = 5
+// with P split everywhere, 5 = warp-specialised two-tile kernel with P in
+// TMEM and register-resident scores, 4 = split softmax (two warps per row
+// set), 3 = one warp per row set reading S from TMEM twice, 2 = as 3 with P
+// in shared memory, 1 = the single-tile kernel. 6 costs no measurable time
+// over 5 on the configs[3] workload (CTAs without a splitting tile run a body
+// compiled without the split).
+std::atomic<int> g_prefill_version{6};
 // Version 6 splits P in query tiles whose first row sees fewer keys than
 // this; over more keys the bf16 roundings of P average out (error ~ 2^-9 x
 // 1.6 / sqrt(keys) per output at unit-variance scores, below 1e-4 here).
