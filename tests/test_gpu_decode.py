@@ -262,3 +262,41 @@ def test_status_word_first_made_under_inference_mode_can_be_cleared():
     assert not word.is_inference()
     assert _lib.read_status(device) == [_lib.STATUS_BITS[2]]
     assert _lib.read_status(device) == []
+
+
+def test_split_partial_ring_wraps_around():
+    """More (row, split) pairs than the split-partial ring holds: 300 rows of
+    7,400-8,192 tokens give ~9,300 pairs against a 4,096-slot ring, so slots
+    are reused (each waits until the row that used it before has merged) and
+    rows' runs of slots straddle the ring's end (split counts of 29-32 do not
+    divide the ring). Every sampled row against the oracle, no status bit
+    (no wait timed out), results deterministic."""
+    rng = np.random.default_rng(12)
+    rows, page, hkv, d = 300, 16, 2, 128
+    lengths = rng.integers(7400, 8193, size=rows).astype(np.int32)
+    pages = [math.ceil(int(n) / page) for n in lengths]
+    width = max(pages)
+    num_blocks = sum(pages)
+    perm = rng.permutation(num_blocks).astype(np.int32)
+    tables = np.full((rows, width), -1, dtype=np.int32)
+    c = 0
+    for r, n in enumerate(pages):
+        tables[r, :n] = perm[c : c + n]
+        c += n
+    key, value = random_pool(num_blocks, 1, page, hkv, d, "bf16", seed=8)
+    g = torch.Generator(device="cuda").manual_seed(9)
+    q = torch.randn((rows, hkv, d), generator=g, device="cuda").to(torch.bfloat16)
+    t = torch.from_numpy(tables).cuda()
+    n = torch.from_numpy(lengths).cuda()
+    splits = [min(math.ceil(int(x) / 256), 128) for x in lengths]
+    assert sum(s for s in splits if s > 1) > 2 * 4096  # wraps the ring twice over
+    backend = rb.B200PagedAttention("cuda", torch.bfloat16, d, page)
+    out = rb.paged_attention(q, key[:, 0], value[:, 0], t, n)
+    torch.cuda.synchronize()
+    assert backend.check_errors() == []
+    sample = sorted(set(rng.choice(rows, 14, replace=False).tolist() + [0, rows - 1]))
+    expected = oracle_rows(q, key[:, 0], value[:, 0], t, lengths, sample, "bf16")
+    assert_close(to_numpy(out[sample]), expected, "bf16")
+    again = rb.paged_attention(q, key[:, 0], value[:, 0], t, n)
+    torch.cuda.synchronize()
+    assert torch.equal(again, out)

@@ -150,24 +150,30 @@ __device__ __forceinline__ int checked_length(const DecodeParams& p, int row, bo
 // Merge the split partials of one query head of one row (one warp): the
 // splits' base-2 running maxima and sums give each split's weight; the output
 // is the weighted sum of the unnormalised accumulators over the total sum.
-// Partial (acc [head_dim], then (max, sum)) of split `sp` of `row` for query
-// head `qh`: element offset of its ring slot's row.
-__device__ __forceinline__ int64_t partial_row(const DecodeParams& p, int row, int sp, int qh) {
-  const int slot = (p.part_base[row] + sp) % p.ring;
-  return static_cast<int64_t>(slot) * p.hq + qh;
-}
-
+//
+// A row's splits occupy consecutive ring slots starting at part_base[row],
+// wrapping past the ring's end at most once, so their partials are two runs
+// with a constant stride; the loops walk each run by a plain stride. (Forming
+// every split's slot with a modulo, or with a wrap test, inside the loop over
+// splits made the merge -- on the critical path of each row's last split --
+// cost the whole decode call 6-10 %.)
 template <typename T>
 __device__ __forceinline__ void merge_splits(const DecodeParams& p, int row, int qh, int count,
                                              int lane) {
+  const int first = p.part_base[row] % p.ring;
+  const int n1 = min(count, p.ring - first);  // splits before the wrap
+  const int64_t stride = p.hq;                // partial rows between consecutive slots
+  const int64_t run1 = static_cast<int64_t>(first) * p.hq + qh;  // split 0
+  const int64_t run2 = qh - static_cast<int64_t>(n1) * p.hq;     // split n1 at slot 0
+  auto at = [&](int sp) { return (sp < n1 ? run1 : run2) + sp * stride; };
   float mx = -INFINITY;
-  for (int sp = lane; sp < count; sp += 32) mx = fmaxf(mx, p.ws_ml[partial_row(p, row, sp, qh) * 2]);
+  for (int sp = lane; sp < count; sp += 32) mx = fmaxf(mx, p.ws_ml[at(sp) * 2]);
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(kFullMask, mx, o));
   const float mref = mx == -INFINITY ? 0.f : mx;
   float total = 0.f;
   for (int sp = lane; sp < count; sp += 32) {
-    const float2 ml = *reinterpret_cast<const float2*>(p.ws_ml + partial_row(p, row, sp, qh) * 2);
+    const float2 ml = *reinterpret_cast<const float2*>(p.ws_ml + at(sp) * 2);
     total += ml.y * ex2(ml.x - mref);
   }
 #pragma unroll
@@ -178,15 +184,19 @@ __device__ __forceinline__ void merge_splits(const DecodeParams& p, int row, int
   T* out = static_cast<T*>(p.out) + row * p.o_rs + qh * p.o_hs;
   for (int d4 = lane; d4 < p.head_dim / 4; d4 += 32) {
     float4 a = make_float4(0.f, 0.f, 0.f, 0.f);
-    for (int sp = 0; sp < count; ++sp) {
-      const int64_t at = partial_row(p, row, sp, qh);
-      const float w = ex2(p.ws_ml[at * 2] - mref);
-      const float4 v = *reinterpret_cast<const float4*>(p.ws_o + at * p.head_dim + d4 * 4);
-      a.x = fmaf(v.x, w, a.x);
-      a.y = fmaf(v.y, w, a.y);
-      a.z = fmaf(v.z, w, a.z);
-      a.w = fmaf(v.w, w, a.w);
-    }
+    auto accumulate = [&](int64_t base, int s0, int s1) {
+      for (int sp = s0; sp < s1; ++sp) {
+        const int64_t r = base + sp * stride;
+        const float w = ex2(p.ws_ml[r * 2] - mref);
+        const float4 v = *reinterpret_cast<const float4*>(p.ws_o + r * p.head_dim + d4 * 4);
+        a.x = fmaf(v.x, w, a.x);
+        a.y = fmaf(v.y, w, a.y);
+        a.z = fmaf(v.z, w, a.z);
+        a.w = fmaf(v.w, w, a.w);
+      }
+    };
+    accumulate(run1, 0, n1);
+    accumulate(run2, n1, count);
     T* dst = out + d4 * 4;
     dst[0] = from_f32<T>(a.x * inv);
     dst[1] = from_f32<T>(a.y * inv);
