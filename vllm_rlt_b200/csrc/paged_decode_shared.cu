@@ -206,8 +206,10 @@ __global__ void __launch_bounds__(kWarps * 32, 4) shared_range_kernel(const Shar
 // 16-bit K/V on the tensor cores (mma.sync m16n8k16, fp32 accumulate): a
 // chunk has at most 32 (member, query head) pairs, one or two 16-row M tiles,
 // far below the 64/128 rows of a tcgen05 tile. The CTA stages 64-token K/V
-// sub-tiles in shared memory (cp.async, double buffered; rows padded to an odd
-// number of 16-byte units so ldmatrix reads are conflict-free). Warp w takes M
+// sub-tiles in shared memory (cp.async, double buffered: the next sub-tile is
+// in flight while one is consumed -- a third buffer measured no faster alone
+// and slowed the suffix decode that runs beside this kernel; rows padded to an
+// odd number of 16-byte units so ldmatrix reads are conflict-free). Warp w takes M
 // tile w % tiles and a slice of every sub-tile's tokens: S = Q K^T (Q
 // fragments stay in registers for the whole chunk, K fragments by ldmatrix),
 // base-2 online softmax on the S fragments (a row's values sit in the 4 lanes
@@ -224,6 +226,7 @@ struct LayoutMma {
   // token-slice merge, reusing the K/V staging: [warp][16 rows][D + 2] floats
   static constexpr int kCombineBytes = kWarps * 16 * (D + 2) * 4;
   static_assert(kCombineBytes <= 2 * 2 * kTileBytes, "merge buffer exceeds the K/V staging");
+  static_assert(2 * (kBytes + 1024) <= 228 * 1024, "two CTAs per SM");
   static_assert((kRowBytes / 16) % 2 == 1, "ldmatrix rows must be an odd number of 16-byte units");
 };
 
@@ -339,54 +342,77 @@ __global__ void __launch_bounds__(kWarps * 32, 2) shared_range_mma_kernel(const 
   const T* kbase = static_cast<const T*>(p.k) + kvh * p.k_hs;
   const T* vbase = static_cast<const T*>(p.v) + kvh * p.v_hs;
   auto tile_ptr = [&](int buf, int which) { return skv + (buf * 2 + which) * L::kTileBytes; };
-  // A thread copies the same 16-byte column v of kPerThread token rows (K
-  // rows, then V rows) of every sub-tile. The page ids of all of them are
-  // read first, as independent loads, and only then are the copies issued:
-  // a table read between each pair of copies put one memory round trip per
-  // copy on this loader's path (the kernel ran at 1.6 TB/s).
+  // Loader: 4 threads per token copy its K row and its V row, each thread a
+  // quarter of both (vector j * 4 + quarter, so the 4 threads of a token read
+  // 64 contiguous bytes per copy); a pass of the CTA covers kPassTokens
+  // tokens. A thread keeps the page index and in-page offset of each of its
+  // tokens and steps them by one sub-tile per call, so a copy costs no
+  // division: per token one address, then 2 x kVecs copies. The page ids a
+  // sub-tile's copies need are read when the previous sub-tile's copies are
+  // issued, so the table's round trip never sits between a warp and its math.
   constexpr int kThreads = kWarps * 32;
-  constexpr int kRowsPerPass = kThreads / kRowVecs;  // token rows one pass of the CTA covers
-  constexpr int kPerThread = 2 * L::kTokens / kRowsPerPass;
-  static_assert(kThreads % kRowVecs == 0 && (2 * L::kTokens) % kRowsPerPass == 0 &&
-                L::kTokens % kRowsPerPass == 0, "loader mapping");
-  const int lv = tid % kRowVecs, lr0 = tid / kRowVecs;
+  constexpr int kQuarter = 4;
+  constexpr int kVecs = kRowVecs / kQuarter;  // 16-byte vectors per thread per row
+  constexpr int kPassTokens = kThreads / kQuarter;
+  constexpr int kPasses = L::kTokens / kPassTokens;
+  static_assert(kRowVecs % kQuarter == 0 && L::kTokens % kPassTokens == 0, "loader mapping");
+  const int quarter = tid % kQuarter, ltok = tid / kQuarter;
   const int64_t trow = static_cast<int64_t>(table_row) * p.t_rs;
-  auto load_tile = [&](int buf, int t0) {
-    int blk[kPerThread];
+  const int step_pages = L::kTokens / p.page, step_off = L::kTokens % p.page;
+  int pg[kPasses], off[kPasses];  // position of token ltok + i * kPassTokens of the next sub-tile
+  int blk[kPasses];               // its page id; INT32_MIN: nothing to read
 #pragma unroll
-    for (int i = 0; i < kPerThread; ++i) {  // K rows i < kPerThread / 2, V rows after
-      const int tok = (lr0 + i * kRowsPerPass) % L::kTokens;
-      const int pos = t0 + tok;
-      const int pg = pos / p.page;
-      blk[i] = INT32_MIN;  // no read: past the chunk or past the table
-      if (pos < tok_end) {
-        if (pg < p.width) {
-          blk[i] = p.tables[trow + pg];
-        } else if (lv == 0) {
+  for (int i = 0; i < kPasses; ++i) {
+    const int pos = tok_begin + ltok + i * kPassTokens;
+    pg[i] = pos / p.page;
+    off[i] = pos % p.page;
+  }
+  auto read_ids = [&](int t0) {
+#pragma unroll
+    for (int i = 0; i < kPasses; ++i) {
+      blk[i] = INT32_MIN;  // past the chunk or past the table
+      if (t0 + ltok + i * kPassTokens < tok_end) {
+        if (pg[i] < p.width) {
+          blk[i] = p.tables[trow + pg[i]];
+        } else if (quarter == 0) {
           raise_status(p.status, kStatusBadLength);
         }
       }
     }
+  };
+  auto load_tile = [&](int buf, int t0) {  // t0: tok_begin, then one sub-tile further per call
 #pragma unroll
-    for (int i = 0; i < kPerThread; ++i) {
-      const int r = lr0 + i * kRowsPerPass;
-      const int which = r / L::kTokens;  // 0: K, 1: V
-      const int tok = r % L::kTokens;
-      const int pos = t0 + tok;
+    for (int i = 0; i < kPasses; ++i) {
+      const int tok = ltok + i * kPassTokens;
       const int b = blk[i];
-      const T* src = which ? vbase : kbase;  // any valid address when nothing is read
+      const T* ks = kbase;  // any valid address when nothing is read
+      const T* vs = vbase;
       uint32_t bytes = 0;
       if (b >= 0 && b < p.num_blocks) {
-        src = which ? vbase + b * p.v_bs + (pos % p.page) * p.v_ts + lv * 8
-                    : kbase + b * p.k_bs + (pos % p.page) * p.k_ts + lv * 8;
+        ks = kbase + b * p.k_bs + off[i] * p.k_ts + quarter * 8;
+        vs = vbase + b * p.v_bs + off[i] * p.v_ts + quarter * 8;
         bytes = 16;
-      } else if (b != INT32_MIN && lv == 0 && which == 0) {
+      } else if (b != INT32_MIN && quarter == 0) {
         raise_status(p.status, kStatusBadBlock);
       }
-      cp_async16(smem_addr(tile_ptr(buf, which) + tok * L::kRowBytes + lv * 16), src, bytes);
+      const uint32_t kd = smem_addr(tile_ptr(buf, 0) + tok * L::kRowBytes + quarter * 16);
+      const uint32_t vd = smem_addr(tile_ptr(buf, 1) + tok * L::kRowBytes + quarter * 16);
+#pragma unroll
+      for (int j = 0; j < kVecs; ++j) {
+        cp_async16(kd + j * kQuarter * 16, ks + (bytes ? j * kQuarter * 8 : 0), bytes);
+        cp_async16(vd + j * kQuarter * 16, vs + (bytes ? j * kQuarter * 8 : 0), bytes);
+      }
+      pg[i] += step_pages;
+      off[i] += step_off;
+      if (off[i] >= p.page) {
+        off[i] -= p.page;
+        ++pg[i];
+      }
     }
     cp_async_commit();
+    read_ids(t0 + L::kTokens);
   };
+  read_ids(tok_begin);
   load_tile(0, tok_begin);
   __syncthreads();  // Q staged
 
@@ -408,8 +434,7 @@ __global__ void __launch_bounds__(kWarps * 32, 2) shared_range_mma_kernel(const 
 
   int buf = 0;
   for (int t0 = tok_begin; t0 < tok_end; t0 += L::kTokens, buf ^= 1) {
-    const bool more = t0 + L::kTokens < tok_end;
-    if (more) {
+    if (t0 + L::kTokens < tok_end) {
       load_tile(buf ^ 1, t0 + L::kTokens);
       cp_async_wait<1>();
     } else {
@@ -472,12 +497,15 @@ __global__ void __launch_bounds__(kWarps * 32, 2) shared_range_mma_kernel(const 
         lrow[e >> 1] += s[j][e];
       }
     }
+    // once the row maxima settle every factor is exactly 1: skip the rescale
+    if (__any_sync(kFullMask, corr[0] != 1.f || corr[1] != 1.f)) {
 #pragma unroll
-    for (int n = 0; n < kDTiles; ++n) {
-      o[n][0] *= corr[0];
-      o[n][1] *= corr[0];
-      o[n][2] *= corr[1];
-      o[n][3] *= corr[1];
+      for (int n = 0; n < kDTiles; ++n) {
+        o[n][0] *= corr[0];
+        o[n][1] *= corr[0];
+        o[n][2] *= corr[1];
+        o[n][3] *= corr[1];
+      }
     }
     // O += P V over the slice's tokens, 16 at a time
     {
