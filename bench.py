@@ -659,7 +659,7 @@ def shared_extra(device, steps, warmup, rank):
         "hbm": {"achieved": round(read / (ms_shared / 1e3) / 1e9, 1), "peak": peak,
                 "unit": "GB/s", "frac": round(read / (ms_shared / 1e3) / 1e9 / peak, 4),
                 "peak_kind": kind, "bytes": "K/V token rows the plan reads, once per group"},
-        "plan_ms_host": round(plan_ms, 2),
+        "plan_ms_host": round(plan_ms, 2), "chunk_tokens": plan.chunk_tokens,
         "errors": backend.check_errors(),
     }
 

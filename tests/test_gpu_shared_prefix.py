@@ -22,7 +22,7 @@ pytestmark = pytest.mark.gpu
 
 
 def run_case(dtype, d, hkv, group, page, rows=12, width=24, groups=((0, 1, 2, 3, 4), (6, 7)),
-             shared=(5, 3), seed=0, empty_rows=()):
+             shared=(5, 3), seed=0, empty_rows=(), chunk_tokens=64):
     tables, lengths, num_blocks = make_case(seed, page=page, rows=rows, width=width, groups=groups,
                                             shared=shared)
     for r in empty_rows:
@@ -36,7 +36,8 @@ def run_case(dtype, d, hkv, group, page, rows=12, width=24, groups=((0, 1, 2, 3,
     q = torch.randn(rows, hkv * group, d, generator=g, device="cuda").to(td)
     t = torch.from_numpy(tables).cuda()
     n = torch.from_numpy(lengths).cuda()
-    plan = rb.plan_shared_prefix(tables, lengths, page, hkv * group, hkv, "cuda", chunk_tokens=64)
+    plan = rb.plan_shared_prefix(tables, lengths, page, hkv * group, hkv, "cuda",
+                                 chunk_tokens=chunk_tokens)
     backend = rb.B200PagedAttention("cuda", td, d, page)
     out = rb.paged_attention_shared(q, key, value, t, plan, context_lengths=n)
     plain = rb.paged_attention(q, key, value, t, n)
@@ -60,6 +61,53 @@ def test_shared_prefix_decode_matches_oracle(dtype, d):
 def test_gqa_and_page_sizes(group, page):
     out, _, expected, _ = run_case("bf16", 128, hkv=2, group=group, page=page, seed=3)
     assert_close(to_numpy(out), expected, "bf16")
+
+
+@pytest.fixture(params=[2, 1], ids=["tma", "cp_async"])
+def staging(request):
+    """The chunk kernel's K/V staging (rlt_shared_prefix_select): 1 = cp.async
+    (the default), 2 = tiled TMA loads where the page size allows."""
+    lib = _lib.load()
+    previous = lib.rlt_shared_prefix_select(request.param)
+    yield request.param
+    lib.rlt_shared_prefix_select(previous)
+
+
+@pytest.mark.parametrize("page,chunk,group,width,shared",
+                         [(16, 512, 1, 24, (20, 12)), (16, 200, 8, 24, (20, 12)),
+                          (8, 100, 1, 40, (30, 20)), (64, 512, 4, 12, (10, 6)),
+                          (48, 512, 2, 24, (20, 12)), (5, 333, 1, 80, (70, 40))])
+def test_chunks_of_many_sub_tiles(page, chunk, group, width, shared, staging):
+    """Chunks longer than one staged sub-tile, including chunk starts inside a
+    page and pages that do not divide the sub-tile (cp.async staging there):
+    the cp.async loader steps each token's page and in-page offset from one
+    sub-tile to the next; the TMA loader starts at the page holding the
+    chunk's first token and masks the tokens outside the chunk."""
+    out, plain, expected, plan = run_case("bf16", 128, hkv=2, group=group, page=page, width=width,
+                                          shared=shared, seed=5, chunk_tokens=chunk)
+    chunks = plan.chunks.cpu().numpy()
+    assert (chunks[:, 2] - chunks[:, 1]).max() > 64
+    assert_close(to_numpy(out), expected, "bf16")
+    assert_close(to_numpy(out), to_numpy(plain), "bf16")
+
+
+@pytest.mark.parametrize("dtype", ["bf16", "f16"])
+@pytest.mark.parametrize("d", [64, 128])
+def test_tma_and_cp_async_staging_agree(dtype, d):
+    """Page-aligned chunks: both stagings put the same tokens in the same
+    sub-tile slices, so their results are bit-identical."""
+    lib = _lib.load()
+    outs = []
+    for mode in (2, 1):
+        previous = lib.rlt_shared_prefix_select(mode)
+        try:
+            out, _, expected, _ = run_case(dtype, d, hkv=2, group=2, page=16, width=24,
+                                           shared=(20, 12), seed=9, chunk_tokens=256)
+        finally:
+            lib.rlt_shared_prefix_select(previous)
+        assert_close(to_numpy(out), expected, dtype)
+        outs.append(out)
+    assert torch.equal(outs[0], outs[1])
 
 
 def test_large_group_split_into_member_blocks_and_empty_rows():

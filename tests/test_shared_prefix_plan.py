@@ -190,3 +190,21 @@ def test_plan_execution_matches_oracle(group):
     got = run_plan(q, key, value, tables, lengths, page, group, chunk_tokens=48)
     want = oracle.paged_attention(q, key, value, tables, lengths, "f32")
     np.testing.assert_allclose(got, want, atol=1e-5, rtol=1e-5)
+
+
+def test_chunk_length_fits_one_resident_wave():
+    """choose_chunk_tokens: the smallest length (512 doubled) whose (chunk, KV
+    head) CTAs fit in one resident wave of the chunk kernel (2 per SM)."""
+    from vllm_rlt_b200.kernels.shared_prefix import choose_chunk_tokens
+
+    # 16 groups of 16 rows sharing 2,560 tokens, 16 KV heads, no GQA
+    groups = [(list(range(16 * g, 16 * g + 16)), 160) for g in range(16)]
+    # 512: 5 x 16 x 16 = 1280 CTAs, 1024: 768, 2048: 512, 4096: 256 <= 296
+    assert choose_chunk_tokens(groups, 16, 1, 16, 148) == 4096
+    assert choose_chunk_tokens(groups, 16, 1, 16, 500) == 1024  # 1000 slots: 768 CTAs
+    # a small shared prefix keeps short chunks (more CTAs for little work)
+    assert choose_chunk_tokens([([0, 1], 100)], 16, 1, 16, 148) == 512
+    # member blocks multiply the CTAs (40 members at group 1 are 2 blocks); no
+    # chunk grows past the longest prefix
+    assert choose_chunk_tokens([(list(range(40)), 64)], 16, 1, 8, 4) == 1024
+    assert choose_chunk_tokens([], 16, 1, 16, 148) == 512

@@ -86,6 +86,7 @@ SIGNATURES = {
         + [_f32, _i32, _p],
     ),
     "rlt_shared_prefix_suffix": (_i32, [_p] * 6 + [_i32] * 3 + [_i64, _p]),
+    "rlt_shared_prefix_select": (_i32, [_i32]),
     "rlt_kv_write": (_i32, [_p] * 7 + [_i32] * 6 + [_i64] * 9 + [_p]),
     "rlt_finalize": (_i32, [_p] * 5 + [_i32] * 8 + [_i64] * 4 + [_p]),
     "rlt_metadata": (_i32, [_p] * 9 + [_i32] * 7 + [_p]),

@@ -20,9 +20,11 @@
 // member_begin, member_count}; members[member_begin + i] = row id;
 // member_slots[...] = the partial slot of that (row, chunk); row_slots[r] ..
 // row_slots[r+1] = the slots of row r. member_count * (Hq / Hkv) <= 32.
+#include <atomic>
 #include <type_traits>
 
 #include "common.cuh"
+#include "tc_ptx.cuh"
 
 namespace rlt {
 namespace {
@@ -35,6 +37,8 @@ constexpr int kPhaseChunks = 1;  // the prefix-chunk partials
 constexpr int kPhaseMerge = 2;   // their merge into the suffix result
 
 struct SharedParams {
+  CUtensorMap kmap;  // kTma chunk kernel: {D, Hkv, page, blocks}, box {64, 1, page, 1}
+  CUtensorMap vmap;
   const void* q;
   const void* k;
   const void* v;
@@ -229,6 +233,28 @@ struct LayoutMma {
   static_assert(2 * (kBytes + 1024) <= 228 * 1024, "two CTAs per SM");
   static_assert((kRowBytes / 16) % 2 == 1, "ldmatrix rows must be an odd number of 16-byte units");
 };
+// TMA staging (kTma chunk kernel): per stage K then V, each [halves of 64
+// dims][64 tokens][128 B] with the 128-byte swizzle (1024-byte aligned);
+// the Q tile (padded rows, as above) and the stage barriers follow.
+template <int D>
+struct LayoutTma {
+  static constexpr int kTokens = 64;
+  static constexpr int kStages = 3;
+  static constexpr int kHalves = D / 64;
+  static constexpr int kHalfBytes = kTokens * 128;         // 64 tokens x 64 dims x 2 B
+  static constexpr int kTileBytes = kHalves * kHalfBytes;  // one K or V sub-tile
+  static constexpr int kStageBytes = 2 * kTileBytes;
+  static constexpr int kQOffset = kStages * kStageBytes;
+  static constexpr int kBarOffset = kQOffset + (LayoutMma<D>::kQBytes + 1023) / 1024 * 1024;
+  static constexpr int kBytes = kBarOffset + kStages * 8 + 1024;  // + alignment slack
+  static constexpr int kCombineBytes = kWarps * 16 * (D + 2) * 4;
+  static_assert(D % 64 == 0, "64-dim halves");
+  static_assert(kCombineBytes <= kStages * kStageBytes, "merge buffer exceeds the K/V staging");
+  static_assert(2 * (kBytes + 1024) <= 228 * 1024, "two CTAs per SM");
+};
+// Bound on a stage wait (cycles, ~50 ms at 1.9 GHz): a load that never lands
+// ends the CTA with RLT_STATUS_TIMEOUT instead of a hang.
+constexpr long long kTmaWaitLimit = 100000000LL;
 
 __device__ __forceinline__ uint32_t smem_addr(const void* ptr) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(ptr));
@@ -293,15 +319,33 @@ __device__ __forceinline__ uint32_t pack_pair<__half>(float lo, float hi) {
   return *reinterpret_cast<uint32_t*>(&v);
 }
 
-template <typename T, int D>
-__global__ void __launch_bounds__(kWarps * 32, 2) shared_range_mma_kernel(const SharedParams p) {
+// 1024-byte aligned start inside the dynamic shared memory (the 128-byte
+// swizzle of a TMA load is a function of the shared-memory address).
+__device__ __forceinline__ uint8_t* align1024(uint8_t* base) {
+  return base + ((1024u - (smem_addr(base) & 1023u)) & 1023u);
+}
+
+// kTma = false: every thread copies its share of each 64-token sub-tile with
+// cp.async from the page table (any page size). kTma = true (pages of 8, 16,
+// 32 or 64 tokens): warp 0's lanes issue one tiled TMA load per page and
+// 64-dim half of K and of V into 128-byte-swizzled stages (three stages, two
+// sub-tiles in flight, bounded mbarrier waits), so no thread spends
+// instructions on copies. The math is the same in both.
+template <typename T, int D, bool kTma>
+__global__ void __launch_bounds__(kWarps * 32, 2)
+    shared_range_mma_kernel(const __grid_constant__ SharedParams p) {
   using L = LayoutMma<D>;
+  using LT = LayoutTma<D>;
   constexpr int kKSteps = D / 16;  // k16 steps over the head dim (S = Q K^T)
   constexpr int kDTiles = D / 8;   // n8 tiles over the head dim (O)
   constexpr int kRowVecs = D / 8;  // 16-byte vectors per row
-  extern __shared__ __align__(16) uint8_t smem[];
-  uint8_t* sq = smem;
-  uint8_t* skv = smem + L::kQBytes;  // [buffer][K, V][token][padded row]
+  constexpr int kTokens = L::kTokens;
+  static_assert(LT::kTokens == kTokens, "one sub-tile size");
+  extern __shared__ __align__(16) uint8_t smem_raw[];
+  uint8_t* smem = kTma ? align1024(smem_raw) : smem_raw;
+  uint8_t* sq = kTma ? smem + LT::kQOffset : smem;
+  uint8_t* skv = kTma ? smem : smem + L::kQBytes;  // K/V staging; later the slice merge
+  uint64_t* bar_full = reinterpret_cast<uint64_t*>(smem + LT::kBarOffset);  // kTma only
 
   const int* c = p.chunks + blockIdx.x * 5;
   const int table_row = c[0], tok_begin = c[1], tok_end = c[2];
@@ -309,56 +353,123 @@ __global__ void __launch_bounds__(kWarps * 32, 2) shared_range_mma_kernel(const 
   const int kvh = blockIdx.y;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int pairs = member_count * p.group;
-  if (pairs <= 0 || pairs > kMaxPairs || tok_begin >= tok_end || table_row < 0 ||
-      table_row >= p.num_rows || member_begin < 0 || member_begin + member_count > p.num_members) {
+  if (pairs <= 0 || pairs > kMaxPairs || tok_begin < 0 || tok_begin >= tok_end ||
+      table_row < 0 || table_row >= p.num_rows || member_begin < 0 ||
+      member_begin + member_count > p.num_members) {
     if (tid == 0 && pairs != 0) raise_status(p.status, kStatusBadSequence);
     return;
   }
   const int tiles = pairs <= 16 ? 1 : 2;
   const int slices = kWarps / tiles;  // 4 or 2 token slices per sub-tile
   const int mt = warp % tiles, sl = warp / tiles;
-  const int slice_tokens = L::kTokens / slices;  // 16 or 32
+  const int slice_tokens = kTokens / slices;  // 16 or 32
   const int g = lane >> 2, tig = lane & 3;
+  const int64_t trow = static_cast<int64_t>(table_row) * p.t_rs;
+  const T* kbase = static_cast<const T*>(p.k) + kvh * p.k_hs;
+  const T* vbase = static_cast<const T*>(p.v) + kvh * p.v_hs;
 
-  // Q of every pair, in the input type (rows >= pairs stay zero)
+  // ---- TMA staging: sub-tile u covers tokens t_first + 64 u ..; page j of
+  // it goes to rows [j * page, (j + 1) * page) of every half of the stage.
+  const int t_first = tok_begin - tok_begin % p.page;  // page-aligned start (kTma)
+  const int n_tiles = (tok_end - t_first + kTokens - 1) / kTokens;
+  const int ppt = kTokens / p.page;  // pages per sub-tile (kTma)
+  // block coordinate of page j of sub-tile u; out of range (zero fill, no
+  // DRAM read) past the chunk or for a bad id
+  auto page_block = [&](int u, int j) {
+    int blk = static_cast<int>(p.num_blocks);
+    const int pos = t_first + u * kTokens + j * p.page;
+    if (pos < tok_end) {
+      const int pg = pos / p.page;
+      if (pg >= p.width) {
+        raise_status(p.status, kStatusBadLength);
+      } else {
+        const int b = p.tables[trow + pg];
+        if (b >= 0 && b < p.num_blocks)
+          blk = b;
+        else
+          raise_status(p.status, kStatusBadBlock);
+      }
+    }
+    return blk;
+  };
+  int next_blk = 0;  // warp 0, lane j < ppt: page j of the next sub-tile to issue, read ahead
+  auto issue = [&](int u) {  // warp 0
+    const int st = u % LT::kStages;
+    if (lane == 0) tc::mbar_expect_tx(&bar_full[st], LT::kStageBytes);
+    __syncwarp();
+    if (lane < ppt) {
+      uint8_t* kd = skv + st * LT::kStageBytes + lane * p.page * 128;
+      uint8_t* vd = kd + LT::kTileBytes;
+#pragma unroll
+      for (int h = 0; h < LT::kHalves; ++h) {
+        tc::tma_load_4d(kd + h * LT::kHalfBytes, &p.kmap, &bar_full[st], h * 64, kvh, 0, next_blk);
+        tc::tma_load_4d(vd + h * LT::kHalfBytes, &p.vmap, &bar_full[st], h * 64, kvh, 0, next_blk);
+      }
+      next_blk = page_block(u + 1, lane);
+    }
+  };
+  if constexpr (kTma) {
+    if (tid == 0) {
+      for (int i = 0; i < LT::kStages; ++i) tc::mbar_init(&bar_full[i], 1);
+      tc::fence_mbar_init();
+    }
+    __syncthreads();
+    if (warp == 0) {
+      if (lane == 0) {
+        tc::prefetch_tensormap(&p.kmap);
+        tc::prefetch_tensormap(&p.vmap);
+      }
+      if (lane < ppt) next_blk = page_block(0, lane);
+      for (int u = 0; u < LT::kStages - 1 && u < n_tiles; ++u) issue(u);
+    }
+  }
+
+  // Q of every pair, in the input type (rows >= pairs stay zero); 16-byte
+  // loads when every row and head starts on a 16-byte boundary
+  const bool q_vec = (reinterpret_cast<uintptr_t>(p.q) & 15) == 0 && p.q_rs % 8 == 0 &&
+                     p.q_hs % 8 == 0;
   for (int e = tid; e < kMaxPairs * kRowVecs; e += kWarps * 32) {
     const int row = e / kRowVecs, v = e % kRowVecs;
-    uint32_t w[4] = {0, 0, 0, 0};
+    uint4 w = make_uint4(0, 0, 0, 0);
     if (row < pairs) {
       const int r = p.members[member_begin + row / p.group];
       const int qh = kvh * p.group + row % p.group;
       if (r >= 0 && r < p.num_rows) {
         const T* src = static_cast<const T*>(p.q) + r * p.q_rs + qh * p.q_hs + v * 8;
+        if (q_vec) {
+          w = *reinterpret_cast<const uint4*>(src);
+        } else {
+          uint32_t x[4];
 #pragma unroll
-        for (int i = 0; i < 4; ++i) {
-          T two[2] = {src[2 * i], src[2 * i + 1]};
-          w[i] = *reinterpret_cast<uint32_t*>(two);
+          for (int i = 0; i < 4; ++i) {
+            T two[2] = {src[2 * i], src[2 * i + 1]};
+            x[i] = *reinterpret_cast<uint32_t*>(two);
+          }
+          w = make_uint4(x[0], x[1], x[2], x[3]);
         }
       }
     }
-    *reinterpret_cast<uint4*>(sq + row * L::kRowBytes + v * 16) = make_uint4(w[0], w[1], w[2], w[3]);
+    *reinterpret_cast<uint4*>(sq + row * L::kRowBytes + v * 16) = w;
   }
 
-  const T* kbase = static_cast<const T*>(p.k) + kvh * p.k_hs;
-  const T* vbase = static_cast<const T*>(p.v) + kvh * p.v_hs;
+  // ---- cp.async staging: 4 threads per token copy its K row and its V row,
+  // each thread a quarter of both (vector j * 4 + quarter, so the 4 threads
+  // of a token read 64 contiguous bytes per copy); a pass of the CTA covers
+  // kPassTokens tokens. A thread keeps the page index and in-page offset of
+  // each of its tokens and steps them by one sub-tile per call, so a copy
+  // costs no division: per token one address, then 2 x kVecs copies. The
+  // page ids a sub-tile's copies need are read when the previous sub-tile's
+  // copies are issued, so the table's round trip never sits between a warp
+  // and its math.
   auto tile_ptr = [&](int buf, int which) { return skv + (buf * 2 + which) * L::kTileBytes; };
-  // Loader: 4 threads per token copy its K row and its V row, each thread a
-  // quarter of both (vector j * 4 + quarter, so the 4 threads of a token read
-  // 64 contiguous bytes per copy); a pass of the CTA covers kPassTokens
-  // tokens. A thread keeps the page index and in-page offset of each of its
-  // tokens and steps them by one sub-tile per call, so a copy costs no
-  // division: per token one address, then 2 x kVecs copies. The page ids a
-  // sub-tile's copies need are read when the previous sub-tile's copies are
-  // issued, so the table's round trip never sits between a warp and its math.
   constexpr int kThreads = kWarps * 32;
   constexpr int kQuarter = 4;
   constexpr int kVecs = kRowVecs / kQuarter;  // 16-byte vectors per thread per row
   constexpr int kPassTokens = kThreads / kQuarter;
-  constexpr int kPasses = L::kTokens / kPassTokens;
-  static_assert(kRowVecs % kQuarter == 0 && L::kTokens % kPassTokens == 0, "loader mapping");
+  constexpr int kPasses = kTokens / kPassTokens;
+  static_assert(kRowVecs % kQuarter == 0 && kTokens % kPassTokens == 0, "loader mapping");
   const int quarter = tid % kQuarter, ltok = tid / kQuarter;
-  const int64_t trow = static_cast<int64_t>(table_row) * p.t_rs;
-  const int step_pages = L::kTokens / p.page, step_off = L::kTokens % p.page;
+  const int step_pages = kTokens / p.page, step_off = kTokens % p.page;
   int pg[kPasses], off[kPasses];  // position of token ltok + i * kPassTokens of the next sub-tile
   int blk[kPasses];               // its page id; INT32_MIN: nothing to read
 #pragma unroll
@@ -410,10 +521,12 @@ __global__ void __launch_bounds__(kWarps * 32, 2) shared_range_mma_kernel(const 
       }
     }
     cp_async_commit();
-    read_ids(t0 + L::kTokens);
+    read_ids(t0 + kTokens);
   };
-  read_ids(tok_begin);
-  load_tile(0, tok_begin);
+  if constexpr (!kTma) {
+    read_ids(tok_begin);
+    load_tile(0, tok_begin);
+  }
   __syncthreads();  // Q staged
 
   // Q fragments of this warp's M tile (matrix j = lane / 8: rows +8 for odd j,
@@ -432,18 +545,17 @@ __global__ void __launch_bounds__(kWarps * 32, 2) shared_range_mma_kernel(const 
   for (int n = 0; n < kDTiles; ++n) o[n][0] = o[n][1] = o[n][2] = o[n][3] = 0.f;
   float mrow[2] = {-INFINITY, -INFINITY}, lrow[2] = {0.f, 0.f};
 
-  int buf = 0;
-  for (int t0 = tok_begin; t0 < tok_end; t0 += L::kTokens, buf ^= 1) {
-    if (t0 + L::kTokens < tok_end) {
-      load_tile(buf ^ 1, t0 + L::kTokens);
-      cp_async_wait<1>();
-    } else {
-      cp_async_wait<0>();
-    }
-    __syncthreads();  // this sub-tile's K and V are in shared memory
+  // shared-memory address of 16-byte chunk cf (over the head dim) of token row tok
+  auto kv_addr = [&](const uint8_t* tile, int tok, int cf) -> uint32_t {
+    if constexpr (kTma)
+      return smem_addr(tile) + (cf >> 3) * LT::kHalfBytes + (tok >> 3) * 1024 + (tok & 7) * 128 +
+             (((cf & 7) ^ (tok & 7)) << 4);
+    else
+      return smem_addr(tile + tok * L::kRowBytes + cf * 16);
+  };
 
-    const uint8_t* ktile = tile_ptr(buf, 0);
-    const uint8_t* vtile = tile_ptr(buf, 1);
+  // one staged sub-tile whose token 0 is t0
+  auto consume = [&](const uint8_t* ktile, const uint8_t* vtile, int t0) {
     const int tok0 = sl * slice_tokens;
     float s[4][4];  // up to 4 n8 token tiles
 #pragma unroll
@@ -456,16 +568,15 @@ __global__ void __launch_bounds__(kWarps * 32, 2) shared_range_mma_kernel(const 
 #pragma unroll
         for (int j = 0; j < 4; j += 2) {
           if (j * 8 >= slice_tokens) break;
-          const uint8_t* a = ktile + (tok0 + (j + (jj >> 1)) * 8 + r) * L::kRowBytes + ks * 32 +
-                             16 * (jj & 1);
           uint32_t b0, b1, b2, b3;
-          ldsm_x4(smem_addr(a), b0, b1, b2, b3);
+          ldsm_x4(kv_addr(ktile, tok0 + (j + (jj >> 1)) * 8 + r, ks * 2 + (jj & 1)), b0, b1, b2,
+                  b3);
           mma16816<T>(s[j], qa[ks], b0, b1);
           mma16816<T>(s[j + 1], qa[ks], b2, b3);
         }
       }
     }
-    // scale, mask the tokens past the chunk, online softmax of rows g and g + 8
+    // scale, mask the tokens outside the chunk, online softmax of rows g and g + 8
     float mx[2] = {-INFINITY, -INFINITY};
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
@@ -473,7 +584,8 @@ __global__ void __launch_bounds__(kWarps * 32, 2) shared_range_mma_kernel(const 
 #pragma unroll
       for (int e = 0; e < 4; ++e) {
         const int tk = t0 + tok0 + j * 8 + 2 * tig + (e & 1);
-        s[j][e] = tk < tok_end ? s[j][e] * p.scale_log2 : -INFINITY;
+        const bool inside = tk < tok_end && (!kTma || tk >= tok_begin);
+        s[j][e] = inside ? s[j][e] * p.scale_log2 : -INFINITY;
         mx[e >> 1] = fmaxf(mx[e >> 1], s[j][e]);
       }
     }
@@ -519,17 +631,64 @@ __global__ void __launch_bounds__(kWarps * 32, 2) shared_range_mma_kernel(const 
         a[2] = pack_pair<T>(s[2 * kk + 1][0], s[2 * kk + 1][1]);
         a[3] = pack_pair<T>(s[2 * kk + 1][2], s[2 * kk + 1][3]);
         // matrix jj: tokens +8 (jj & 1), dim tile +(jj >> 1)
-        const uint8_t* vrow = vtile + (tok0 + kk * 16 + 8 * (jj & 1) + r) * L::kRowBytes;
+        const int vtok = tok0 + kk * 16 + 8 * (jj & 1) + r;
 #pragma unroll
         for (int n = 0; n < kDTiles; n += 2) {
           uint32_t b0, b1, b2, b3;
-          ldsm_x4_t(smem_addr(vrow + (n + (jj >> 1)) * 16), b0, b1, b2, b3);
+          ldsm_x4_t(kv_addr(vtile, vtok, n + (jj >> 1)), b0, b1, b2, b3);
           mma16816<T>(o[n], a, b0, b1);
           mma16816<T>(o[n + 1], a, b2, b3);
         }
       }
     }
-    __syncthreads();  // every warp is done with this buffer before it is refilled
+  };
+
+  if constexpr (kTma) {
+    for (int t = 0; t < n_tiles; ++t) {
+      const int st = t % LT::kStages;
+      const bool ok = tc::mbar_wait(&bar_full[st], (t / LT::kStages) & 1, kTmaWaitLimit);
+      uint8_t* ktile = skv + st * LT::kStageBytes;
+      uint8_t* vtile = ktile + LT::kTileBytes;
+      const int t0 = t_first + t * kTokens;
+      const int valid = tok_end - t0;
+      if (ok && valid < kTokens) {
+        // V rows past the chunk may hold any bits (NaN included) and P is 0
+        // there: zero them so P V stays finite (the TMA writes have landed)
+        for (int e = tid; e < (kTokens - valid) * LT::kHalves * 8; e += kWarps * 32) {
+          const int tok = valid + e / (LT::kHalves * 8);
+          const int h = (e / 8) % LT::kHalves, cidx = e % 8;
+          *reinterpret_cast<uint4*>(vtile + h * LT::kHalfBytes + (tok >> 3) * 1024 +
+                                    (tok & 7) * 128 + cidx * 16) = make_uint4(0, 0, 0, 0);
+        }
+      }
+      // this sub-tile has landed everywhere, and every warp is done with the
+      // stage the next load refills (it held sub-tile t - 1)
+      if (__syncthreads_or(!ok)) {
+        if (tid == 0) {
+          raise_status(p.status, kStatusTimeout);
+          // let the loads in flight land before the CTA's shared memory goes
+          for (int u = t; u < n_tiles && u < t + LT::kStages - 1; ++u)
+            tc::mbar_wait(&bar_full[u % LT::kStages], (u / LT::kStages) & 1, kTmaWaitLimit);
+        }
+        return;
+      }
+      if (warp == 0 && t + LT::kStages - 1 < n_tiles) issue(t + LT::kStages - 1);
+      consume(ktile, vtile, t0);
+    }
+    __syncthreads();  // every warp is done with the last stage before the merge reuses it
+  } else {
+    int buf = 0;
+    for (int t0 = tok_begin; t0 < tok_end; t0 += kTokens, buf ^= 1) {
+      if (t0 + kTokens < tok_end) {
+        load_tile(buf ^ 1, t0 + kTokens);
+        cp_async_wait<1>();
+      } else {
+        cp_async_wait<0>();
+      }
+      __syncthreads();  // this sub-tile's K and V are in shared memory
+      consume(tile_ptr(buf, 0), tile_ptr(buf, 1), t0);
+      __syncthreads();  // every warp is done with this buffer before it is refilled
+    }
   }
 
 #pragma unroll
@@ -537,63 +696,63 @@ __global__ void __launch_bounds__(kWarps * 32, 2) shared_range_mma_kernel(const 
     lrow[h] += __shfl_xor_sync(kFullMask, lrow[h], 1);
     lrow[h] += __shfl_xor_sync(kFullMask, lrow[h], 2);
   }
-  // merge the token slices of each M tile (the K/V staging is free now)
+  // merge the token slices of each M tile (the K/V staging is free now):
+  // every warp stores its partial rows, then each warp merges a quarter of
+  // the columns of every pair
+  constexpr int kCbRow = D + 2;  // floats per staged row: o, then max and sum
   float* cb = reinterpret_cast<float*>(skv);
   {
-    float* mine = cb + warp * 16 * (D + 2);
+    float* mine = cb + warp * 16 * kCbRow;
 #pragma unroll
     for (int n = 0; n < kDTiles; ++n) {
       const int col = n * 8 + 2 * tig;
-      mine[g * (D + 2) + col] = o[n][0];
-      mine[g * (D + 2) + col + 1] = o[n][1];
-      mine[(g + 8) * (D + 2) + col] = o[n][2];
-      mine[(g + 8) * (D + 2) + col + 1] = o[n][3];
+      *reinterpret_cast<float2*>(mine + g * kCbRow + col) = make_float2(o[n][0], o[n][1]);
+      *reinterpret_cast<float2*>(mine + (g + 8) * kCbRow + col) = make_float2(o[n][2], o[n][3]);
     }
     if (tig == 0) {
-      mine[g * (D + 2) + D] = mrow[0];
-      mine[g * (D + 2) + D + 1] = lrow[0];
-      mine[(g + 8) * (D + 2) + D] = mrow[1];
-      mine[(g + 8) * (D + 2) + D + 1] = lrow[1];
+      *reinterpret_cast<float2*>(mine + g * kCbRow + D) = make_float2(mrow[0], lrow[0]);
+      *reinterpret_cast<float2*>(mine + (g + 8) * kCbRow + D) = make_float2(mrow[1], lrow[1]);
     }
   }
   __syncthreads();
-  if (sl != 0) return;
-  // warp (slice 0, tile mt): lane covers rows g, g + 8 and its columns
-#pragma unroll
-  for (int h = 0; h < 2; ++h) {
-    const int row = g + 8 * h;
-    const int pair = mt * 16 + row;
+  constexpr int kChunkCols = 8;                             // columns per work item
+  constexpr int kItemsPerRow = D / kWarps / kChunkCols;     // items of one pair in one warp
+  static_assert(D % (kWarps * kChunkCols) == 0, "epilogue column split");
+  for (int it = lane; it < tiles * 16 * kItemsPerRow; it += 32) {
+    const int pair = it / kItemsPerRow;  // = M tile * 16 + row
+    const int col = (warp * kItemsPerRow + it % kItemsPerRow) * kChunkCols;
+    if (pair >= pairs) continue;
+    const int tile = pair / 16, row = pair % 16;
     float mxs = -INFINITY;
     for (int k = 0; k < slices; ++k)
-      mxs = fmaxf(mxs, cb[((k * tiles + mt) * 16 + row) * (D + 2) + D]);
+      mxs = fmaxf(mxs, cb[((k * tiles + tile) * 16 + row) * kCbRow + D]);
     const float mref = mxs == -INFINITY ? 0.f : mxs;
-    float wk[kWarps];
+    float acc[kChunkCols];
+#pragma unroll
+    for (int e = 0; e < kChunkCols; ++e) acc[e] = 0.f;
     float lsum = 0.f;
     for (int k = 0; k < slices; ++k) {
-      const float* st = cb + ((k * tiles + mt) * 16 + row) * (D + 2);
-      wk[k] = ex2(st[D] - mref);
-      lsum += st[D + 1] * wk[k];
+      const float* st = cb + ((k * tiles + tile) * 16 + row) * kCbRow;
+      const float w = ex2(st[D] - mref);
+      lsum += st[D + 1] * w;
+#pragma unroll
+      for (int e = 0; e < kChunkCols; e += 2) {
+        const float2 x = *reinterpret_cast<const float2*>(st + col + e);
+        acc[e] = fmaf(x.x, w, acc[e]);
+        acc[e + 1] = fmaf(x.y, w, acc[e + 1]);
+      }
     }
-    if (pair >= pairs) continue;
     const int slot = p.member_slots[member_begin + pair / p.group];
     if (slot < 0 || slot >= p.num_slots) {
-      if (tig == 0) raise_status(p.status, kStatusBadSequence);
+      if (col == 0) raise_status(p.status, kStatusBadSequence);
       continue;
     }
     const int qh = kvh * p.group + pair % p.group;
-    float* dst = p.ws_o + (static_cast<int64_t>(slot) * p.hq + qh) * D;
+    float4* dst = reinterpret_cast<float4*>(p.ws_o + (static_cast<int64_t>(slot) * p.hq + qh) * D + col);
 #pragma unroll
-    for (int n = 0; n < kDTiles; ++n) {
-#pragma unroll
-      for (int e = 0; e < 2; ++e) {
-        const int col = n * 8 + 2 * tig + e;
-        float acc = 0.f;
-        for (int k = 0; k < slices; ++k)
-          acc = fmaf(cb[((k * tiles + mt) * 16 + row) * (D + 2) + col], wk[k], acc);
-        dst[col] = acc;
-      }
-    }
-    if (tig == 0) {
+    for (int e = 0; e < kChunkCols; e += 4)
+      dst[e / 4] = make_float4(acc[e], acc[e + 1], acc[e + 2], acc[e + 3]);
+    if (col == 0) {
       float* ml = p.ws_ml + (static_cast<int64_t>(slot) * p.hq + qh) * 2;
       ml[0] = mxs;
       ml[1] = lsum;
@@ -671,7 +830,7 @@ size_t workspace_bytes(int64_t slots, int hq, int d) {
 }
 
 template <typename T, int D>
-int launch(const SharedParams& p, int num_chunks, const int32_t* row_slots,
+int launch(const SharedParams& p, bool tma, int num_chunks, const int32_t* row_slots,
            const float* suffix_lse, void* out, int64_t o_rs, int64_t o_hs, int phases,
            cudaStream_t stream) {
   if (!(phases & kPhaseChunks)) {
@@ -683,13 +842,22 @@ int launch(const SharedParams& p, int num_chunks, const int32_t* row_slots,
     if (attr != cudaSuccess) return static_cast<int>(attr);
     if (num_chunks > 0)
       shared_range_kernel<T, D><<<dim3(num_chunks, p.hkv), kWarps * 32, bytes, stream>>>(p);
+  } else if (tma) {
+    constexpr int bytes = LayoutTma<D>::kBytes;
+    static cudaError_t attr = cudaFuncSetAttribute(
+        shared_range_mma_kernel<T, D, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+    if (attr != cudaSuccess) return static_cast<int>(attr);
+    if (num_chunks > 0)
+      shared_range_mma_kernel<T, D, true>
+          <<<dim3(num_chunks, p.hkv), kWarps * 32, bytes, stream>>>(p);
   } else {
     constexpr int bytes = LayoutMma<D>::kBytes;
     static cudaError_t attr = cudaFuncSetAttribute(
-        shared_range_mma_kernel<T, D>, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+        shared_range_mma_kernel<T, D, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
     if (attr != cudaSuccess) return static_cast<int>(attr);
     if (num_chunks > 0)
-      shared_range_mma_kernel<T, D><<<dim3(num_chunks, p.hkv), kWarps * 32, bytes, stream>>>(p);
+      shared_range_mma_kernel<T, D, false>
+          <<<dim3(num_chunks, p.hkv), kWarps * 32, bytes, stream>>>(p);
   }
   if ((phases & kPhaseMerge) && p.num_rows > 0)
     shared_merge_kernel<T, D><<<dim3(p.num_rows, ceil_div(p.hq, kWarps)), kWarps * 32, 0, stream>>>(
@@ -697,12 +865,33 @@ int launch(const SharedParams& p, int num_chunks, const int32_t* row_slots,
   return launch_status(cudaGetLastError());
 }
 
+// 1 (default): 16-bit chunks are staged by cp.async; 2: by TMA where the page
+// allows it. TMA staging makes the chunk kernel alone ~8 % faster (configs[1]
+// prefix-cached batch: 87 us against 95 us), but beside the suffix decode the
+// call measured 314-340 us against 261-287 us with cp.async staging (the
+// resident mix of the two kernels' CTAs on an SM differs), so the overlapped
+// call keeps cp.async.
+std::atomic<int> g_shared_staging{1};
+
 bool aligned16(const void* ptr) { return (reinterpret_cast<uintptr_t>(ptr) & 15u) == 0; }
 
 }  // namespace
 }  // namespace rlt
 
+namespace rlt {
+namespace detail {
+bool encode_kv_page_map(CUtensorMap* map, int32_t dtype, const void* base, int32_t head_dim,
+                        int32_t hkv, int32_t page, int64_t num_blocks, int64_t bs, int64_t ts,
+                        int64_t hs);
+}  // namespace detail
+}  // namespace rlt
+
 using namespace rlt;
+
+extern "C" int rlt_shared_prefix_select(int32_t staging) {
+  if (staging != 1 && staging != 2) return g_shared_staging.load();
+  return g_shared_staging.exchange(staging);
+}
 
 extern "C" size_t rlt_paged_decode_shared_workspace_bytes(int32_t num_slots, int32_t num_q_heads,
                                                           int32_t head_dim) {
@@ -786,23 +975,36 @@ int shared_entry(
   p.t_rs = table_row_stride;
   p.scale_log2 = scale * 1.4426950408889634f;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
+  // TMA staging: whole pages of 8..64 tokens tile a 64-token sub-tile, each
+  // page's box lands 1024-byte aligned in the swizzled stage
+  bool tma = false;
+  if (dtype != RLT_F32 && (phases & kPhaseChunks) && num_chunks > 0 &&
+      g_shared_staging.load() == 2 &&
+      (page_size == 8 || page_size == 16 || page_size == 32 || page_size == 64) &&
+      num_blocks > 0 && num_blocks < INT32_MAX)
+    tma = detail::encode_kv_page_map(&p.kmap, dtype, key_cache, head_dim, num_kv_heads,
+                                     page_size, num_blocks, k_block_stride, k_token_stride,
+                                     k_head_stride) &&
+          detail::encode_kv_page_map(&p.vmap, dtype, value_cache, head_dim, num_kv_heads,
+                                     page_size, num_blocks, v_block_stride, v_token_stride,
+                                     v_head_stride);
   const bool d128 = head_dim == 128;
   switch (dtype) {
     case RLT_BF16:
-      return d128 ? launch<__nv_bfloat16, 128>(p, num_chunks, row_slots, suffix_lse, out, out_row_stride,
-                                               out_head_stride, phases, s)
-                  : launch<__nv_bfloat16, 64>(p, num_chunks, row_slots, suffix_lse, out, out_row_stride,
-                                              out_head_stride, phases, s);
+      return d128 ? launch<__nv_bfloat16, 128>(p, tma, num_chunks, row_slots, suffix_lse, out,
+                                               out_row_stride, out_head_stride, phases, s)
+                  : launch<__nv_bfloat16, 64>(p, tma, num_chunks, row_slots, suffix_lse, out,
+                                              out_row_stride, out_head_stride, phases, s);
     case RLT_F16:
-      return d128 ? launch<__half, 128>(p, num_chunks, row_slots, suffix_lse, out, out_row_stride,
-                                        out_head_stride, phases, s)
-                  : launch<__half, 64>(p, num_chunks, row_slots, suffix_lse, out, out_row_stride,
-                                       out_head_stride, phases, s);
+      return d128 ? launch<__half, 128>(p, tma, num_chunks, row_slots, suffix_lse, out,
+                                        out_row_stride, out_head_stride, phases, s)
+                  : launch<__half, 64>(p, tma, num_chunks, row_slots, suffix_lse, out,
+                                       out_row_stride, out_head_stride, phases, s);
     default:
-      return d128 ? launch<float, 128>(p, num_chunks, row_slots, suffix_lse, out, out_row_stride,
-                                       out_head_stride, phases, s)
-                  : launch<float, 64>(p, num_chunks, row_slots, suffix_lse, out, out_row_stride,
-                                      out_head_stride, phases, s);
+      return d128 ? launch<float, 128>(p, false, num_chunks, row_slots, suffix_lse, out,
+                                       out_row_stride, out_head_stride, phases, s)
+                  : launch<float, 64>(p, false, num_chunks, row_slots, suffix_lse, out,
+                                      out_row_stride, out_head_stride, phases, s);
   }
 }
 }  // namespace

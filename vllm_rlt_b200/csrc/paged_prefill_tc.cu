@@ -1383,6 +1383,23 @@ namespace detail {
 
 constexpr int kNotEligible = 1;
 
+// A 4-D tiled tensor map over one layer view of a KV pool, [blocks, page,
+// Hkv, D] with element strides (bs, ts, hs), box {64, 1, page, 1}, 128-byte
+// swizzle: one TMA load brings 64 head dims of one KV head for every token
+// of one page. False when the driver rejects the shape or strides.
+bool encode_kv_page_map(CUtensorMap* map, int32_t dtype, const void* base, int32_t head_dim,
+                        int32_t hkv, int32_t page, int64_t num_blocks, int64_t bs, int64_t ts,
+                        int64_t hs) {
+  const CUtensorMapDataType type =
+      dtype == RLT_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+  const uint64_t dims[4] = {static_cast<uint64_t>(head_dim), static_cast<uint64_t>(hkv),
+                            static_cast<uint64_t>(page), static_cast<uint64_t>(num_blocks)};
+  const uint64_t strides[3] = {static_cast<uint64_t>(hs) * 2, static_cast<uint64_t>(ts) * 2,
+                               static_cast<uint64_t>(bs) * 2};
+  const uint32_t box[4] = {64, 1, static_cast<uint32_t>(page), 1};
+  return encode(map, type, 4, base, dims, strides, box);
+}
+
 bool prefill_tc_shape(int32_t dtype, int32_t head_dim, int32_t page) {
   return (dtype == RLT_BF16 || dtype == RLT_F16) && head_dim == kHeadDim &&
          (page == 8 || page == 16 || page == 32 || page == 64 || page == 128);

@@ -81,21 +81,25 @@ class SharedPrefixPlan:
     groups: list = field(default_factory=list)
     logical_tokens: int = 0     # sum of context lengths (token rows a per-row decode reads)
     read_tokens: int = 0        # token rows this plan reads (per KV head)
+    chunk_tokens: int = 0       # longest token range of one chunk
 
 
-def plan_arrays(tables, lengths, page: int, group: int, chunk_tokens: int = 256, min_rows: int = 2):
+def plan_arrays(tables, lengths, page: int, group: int, chunk_tokens: int = 256, min_rows: int = 2,
+                groups=None):
     """Host plan as numpy arrays: (chunks [C,5], members, member_slots,
     row_slots, suffix_tables, suffix_lengths, groups, logical_tokens,
     read_tokens). ``group`` = query heads per KV head (GQA). The chunks cover
     the shared prefixes; row r's tokens [prefix_r, ctx_r) are read through
-    suffix_tables[r] (tokens renumbered from 0)."""
+    suffix_tables[r] (tokens renumbered from 0). ``groups``: the rows'
+    ``find_shared_prefixes`` result when the caller already has it."""
     tables = np.asarray(tables)
     lengths = np.asarray(lengths, dtype=np.int64)
     rows = tables.shape[0]
     if group < 1 or group > MAX_PAIRS:
         raise ValueError(f"query heads per KV head must be in [1, {MAX_PAIRS}]")
     max_members = MAX_PAIRS // group
-    groups = find_shared_prefixes(tables, lengths, page, min_rows)
+    if groups is None:
+        groups = find_shared_prefixes(tables, lengths, page, min_rows)
     prefix = np.zeros(rows, dtype=np.int64)
     items = []  # (table row, begin, end, member rows)
     for members, shared in groups:
@@ -134,17 +138,58 @@ def plan_arrays(tables, lengths, page: int, group: int, chunk_tokens: int = 256,
             int(lengths.clip(min=0).sum()), int(read_tokens))
 
 
+# Chunk CTAs one SM holds at once (the chunk kernel's launch bounds).
+CHUNK_CTAS_PER_SM = 2
+
+
+def choose_chunk_tokens(groups, page: int, group: int, num_kv_heads: int, num_sms: int,
+                        smallest: int = 512) -> int:
+    """The smallest chunk length (``smallest`` doubled until it fits) whose
+    (chunk, KV head) CTAs fit in one resident wave of the chunk kernel.
+
+    The chunk kernel runs beside the suffix decode, and one resident wave of
+    long chunks leaves the decode the SMs' remaining slots for the whole call:
+    on the prefix-cached configs[1] batch (16 groups of 16 rows, 1-4K shared
+    tokens) the overlapped call took 287 us with 512-token chunks, 265 us with
+    2048 and 261 us with 4096 (one wave), while the chunk kernel alone is
+    fastest with many short chunks."""
+    max_members = MAX_PAIRS // group
+    work = [(int(shared) * page, -(-len(members) // max_members)) for members, shared in groups]
+    slots = CHUNK_CTAS_PER_SM * max(1, int(num_sms))
+    chunk = smallest
+    longest = max((tokens for tokens, _ in work), default=smallest)
+    while chunk < longest:
+        ctas = sum(-(-tokens // chunk) * blocks for tokens, blocks in work) * num_kv_heads
+        if ctas <= slots:
+            break
+        chunk *= 2
+    return chunk
+
+
+def _num_sms(device) -> int:
+    device = torch.device(device)
+    if device.type == "cuda" and torch.cuda.is_available():
+        return torch.cuda.get_device_properties(device).multi_processor_count
+    return 148  # B200
+
+
 def plan_shared_prefix(block_tables, context_lengths, page_size: int, num_q_heads: int,
-                       num_kv_heads: int, device, chunk_tokens: int = 512) -> SharedPrefixPlan:
+                       num_kv_heads: int, device, chunk_tokens: int | None = None) -> SharedPrefixPlan:
     """Build the plan on the host (tables/lengths may be tensors on any
-    device or numpy arrays) and upload it to ``device``."""
+    device or numpy arrays) and upload it to ``device``. ``chunk_tokens``
+    None picks the chunk length with ``choose_chunk_tokens``."""
     tables = block_tables.cpu().numpy() if torch.is_tensor(block_tables) else np.asarray(block_tables)
     lengths = (context_lengths.cpu().numpy() if torch.is_tensor(context_lengths)
                else np.asarray(context_lengths))
     if num_q_heads % num_kv_heads:
         raise ValueError("query heads must be a positive multiple of KV heads")
+    groups = find_shared_prefixes(tables, np.asarray(lengths, dtype=np.int64), page_size)
+    if chunk_tokens is None:
+        chunk_tokens = choose_chunk_tokens(groups, page_size, num_q_heads // num_kv_heads,
+                                           num_kv_heads, _num_sms(device))
     (chunks, members, slots, row_slots, suffix_tables, suffix_lengths, groups, logical,
-     read) = plan_arrays(tables, lengths, page_size, num_q_heads // num_kv_heads, chunk_tokens)
+     read) = plan_arrays(tables, lengths, page_size, num_q_heads // num_kv_heads, chunk_tokens,
+                         groups=groups)
 
     def up(a):
         return torch.from_numpy(np.ascontiguousarray(a)).to(device)
@@ -157,7 +202,7 @@ def plan_shared_prefix(block_tables, context_lengths, page_size: int, num_q_head
         suffix_tables=up(suffix_tables), suffix_lengths=up(suffix_lengths),
         prefix_pages=up(prefix_pages), lengths=up(clipped.astype(np.int32)),
         num_rows=int(tables.shape[0]), num_chunks=int(len(chunks)), num_slots=int(row_slots[-1]),
-        groups=groups, logical_tokens=logical, read_tokens=read)
+        groups=groups, logical_tokens=logical, read_tokens=read, chunk_tokens=int(chunk_tokens))
 
 
 _SIDE_STREAMS = {}
