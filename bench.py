@@ -274,6 +274,41 @@ def reference_cpu_sample(plan, budget_s):
     return HostDecode(plan, rows), fn, kind, label, threads
 
 
+def cpu_model() -> str:
+    """The host CPU's model name (Linux /proc/cpuinfo), for the baseline lines."""
+    try:
+        with open("/proc/cpuinfo") as f:
+            for line in f:
+                if line.startswith("model name"):
+                    return line.split(":", 1)[1].strip()
+    except OSError:
+        pass
+    return "unknown"
+
+
+def single_thread_rate(plan, fn, budget_s=3.0):
+    """The reference's CPU path on one host thread (torch.set_num_threads(1)):
+    GB/s over a seeded 4-row sample, repeated for about ``budget_s`` seconds."""
+    import torch
+
+    before = torch.get_num_threads()
+    torch.set_num_threads(1)
+    try:
+        rows = [int(r) for r in np.random.default_rng(321).permutation(plan.num_rows)[:4]]
+        host = HostDecode(plan, rows, seed=1)
+        host.run(fn)
+        reps, spent = 0, 0.0
+        while spent < budget_s and reps < 20:
+            t0 = time.perf_counter()
+            host.run(fn)
+            spent += time.perf_counter() - t0
+            reps += 1
+        return {"value": round(host.bytes * reps / spent / 1e9, 3), "unit": "GB/s", "cores": 1,
+                "sample": f"{len(rows)} rows (sum ctx {host.tokens}) x {reps} calls"}
+    finally:
+        torch.set_num_threads(before)
+
+
 def reference_kv_cpu(batch=64, reps=20):
     """BASELINE B4: the reference's CPU KVCacheManager.write (one layer, a
     batch of rows) and finalize_token (one token, every layer, into the deeper
@@ -383,7 +418,8 @@ def run_reference(args):
                     "sum_ctx_per_gpu": host.tokens, "bytes_per_step_per_gpu": int(host.bytes),
                     "sample": sample}),
         "cpu_baseline": {"value": round(value, 3), "unit": "GB/s", "cores": threads,
-                         "kind": kind, "sample": sample},
+                         "kind": kind, "sample": sample, "cpu_model": cpu_model(),
+                         "single_thread": single_thread_rate(plan, fn)},
         "e2e": {"value": round(value, 3), "unit": "GB/s", "h2d_bytes_per_step": 0,
                 "d2h_bytes_per_step": 0},
         "reference_kv_cpu": reference_kv_cpu(),
@@ -1144,6 +1180,8 @@ def run_ours(args):
             "cores": threads, "kind": kind,
             "sample": (f"{len(host.rows)} of {plan.num_rows} rows (sum ctx {host.tokens}) x "
                        f"{reps} calls; {label}"),
+            "cpu_model": cpu_model(), "host_threads": os.cpu_count(),
+            "single_thread": single_thread_rate(plan, fn),
             "reference_kv_cpu": reference_kv_cpu(),
         }
         del host
