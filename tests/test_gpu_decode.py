@@ -133,6 +133,25 @@ def test_split_boundaries_and_long_rows_vs_oracle():
     assert_close(to_numpy(out), expected, "bf16")
 
 
+def test_batch_beyond_one_schedule_pass_vs_oracle():
+    """2,500 rows: the one-CTA schedule kernel orders and scans the rows in
+    three passes of 1,024 (batches up to 1,024 rows take its one-pass path);
+    sampled rows of every split count, including the first and last scheduled,
+    against the oracle, and the same rows alone through a one-pass call."""
+    rng = np.random.default_rng(5)
+    lengths = rng.integers(1, 1200, size=2500).astype(np.int32)
+    lengths[[3, 1700, 2499]] = [9000, 4500, 257]
+    q, k, v, tables, lengths_t, out = run_case(len(lengths), 4, 2, 128, 16, "bf16", lengths,
+                                               layers=1, layer=0, seed=3)
+    picks = sorted(set([0, 3, 1023, 1024, 1700, 2047, 2048, 2499]
+                       + rng.choice(len(lengths), 24, replace=False).tolist()))
+    expected = oracle_rows(q, k, v, tables, lengths_t, picks, "bf16")
+    assert_close(to_numpy(out[picks]), expected, "bf16")
+    idx = torch.tensor(picks, device="cuda")
+    alone = rb.paged_attention(q[idx], k, v, tables[idx], lengths_t[idx])
+    assert torch.equal(alone, out[idx])
+
+
 def test_fp32_long_rows_vs_oracle():
     lengths = [1, 300, 1000, 4097]
     q, k, v, tables, lengths_t, out = run_case(len(lengths), 16, 16, 128, 16, "f32", lengths,

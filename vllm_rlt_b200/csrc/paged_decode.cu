@@ -595,10 +595,16 @@ __device__ __forceinline__ int scheduled_splits(const DecodeParams& p, int r) {
 __global__ void __launch_bounds__(kScheduleThreads) decode_schedule_kernel(
     const __grid_constant__ DecodeParams p, int blocks_per_row, int* counters, int* schedule,
     int* work) {
-  __shared__ int scan[kScheduleThreads];
-  __shared__ int pscan[kScheduleThreads];
+  constexpr int kScheduleWarps = kScheduleThreads / 32;
+  static_assert(kScheduleWarps <= 32, "warp totals scanned by one warp");
+  __shared__ int wsum[kScheduleWarps], wpsum[kScheduleWarps];  // per-warp inclusive totals
   __shared__ int bucket[kMaxSplits + 1];  // rows per split count, then placement cursors
-  const int tid = threadIdx.x;
+  // one pass (rows <= kScheduleThreads): the scan reads the order and the
+  // split counts from here instead of a global round trip
+  __shared__ int s_order[kScheduleThreads], s_splits[kScheduleThreads];
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const bool one_pass = p.rows <= kScheduleThreads;
+  const int my_splits = one_pass && tid < p.rows ? scheduled_splits(p, tid) : 0;
   const int64_t ncounters = static_cast<int64_t>(p.rows) * p.hq;
   for (int64_t i = tid; i < ncounters; i += kScheduleThreads) counters[i] = 0;
   for (int i = tid; i < p.rows; i += kScheduleThreads) p.row_merges[i] = 0;
@@ -606,20 +612,49 @@ __global__ void __launch_bounds__(kScheduleThreads) decode_schedule_kernel(
   for (int i = tid; i <= kMaxSplits; i += kScheduleThreads) bucket[i] = 0;
   if (tid == 0) *work = 0;
   __syncthreads();
-  for (int r = tid; r < p.rows; r += kScheduleThreads) atomicAdd(&bucket[scheduled_splits(p, r)], 1);
+  if (one_pass) {
+    if (tid < p.rows) atomicAdd(&bucket[my_splits], 1);
+  } else {
+    for (int r = tid; r < p.rows; r += kScheduleThreads) atomicAdd(&bucket[scheduled_splits(p, r)], 1);
+  }
   __syncthreads();
-  if (tid == 0) {  // first position of each split count, most splits first
-    int at = 0;
-    for (int c = kMaxSplits; c >= 0; --c) {
-      const int n = bucket[c];
-      bucket[c] = at;
-      at += n;
+  if (warp == 0) {  // first position of each split count, most splits first
+    // lane l holds counts kMaxSplits - 5 l ... kMaxSplits - 5 l - 4
+    constexpr int kPer = (kMaxSplits + 1 + 31) / 32;
+    int n[kPer], sum = 0;
+#pragma unroll
+    for (int i = 0; i < kPer; ++i) {
+      const int c = kMaxSplits - (lane * kPer + i);
+      n[i] = c >= 0 ? bucket[c] : 0;
+      sum += n[i];
+    }
+    int incl = sum;
+#pragma unroll
+    for (int off = 1; off < 32; off <<= 1) {
+      const int y = __shfl_up_sync(kFullMask, incl, off);
+      if (lane >= off) incl += y;
+    }
+    int at = incl - sum;
+#pragma unroll
+    for (int i = 0; i < kPer; ++i) {
+      const int c = kMaxSplits - (lane * kPer + i);
+      if (c >= 0) bucket[c] = at;
+      at += n[i];
     }
   }
   __syncthreads();
   int* order = const_cast<int*>(p.order);
-  for (int r = tid; r < p.rows; r += kScheduleThreads)
-    order[RLT_DECODE_LPT ? atomicAdd(&bucket[scheduled_splits(p, r)], 1) : r] = r;
+  if (one_pass) {
+    if (tid < p.rows) {
+      const int at = RLT_DECODE_LPT ? atomicAdd(&bucket[my_splits], 1) : tid;
+      order[at] = tid;
+      s_order[at] = tid;
+      s_splits[at] = my_splits;
+    }
+  } else {
+    for (int r = tid; r < p.rows; r += kScheduleThreads)
+      order[RLT_DECODE_LPT ? atomicAdd(&bucket[scheduled_splits(p, r)], 1) : r] = r;
+  }
   __syncthreads();  // the order is visible to the whole CTA
   int carry = 0, pcarry = 0;
   int* part_base = const_cast<int*>(p.part_base);
@@ -627,29 +662,57 @@ __global__ void __launch_bounds__(kScheduleThreads) decode_schedule_kernel(
     const int q = base + tid;
     int items = 0, pairs = 0, r = 0;
     if (q < p.rows) {
-      r = order[q];
-      const int count = scheduled_splits(p, r);
+      r = one_pass ? s_order[q] : order[q];
+      const int count = one_pass ? s_splits[q] : scheduled_splits(p, r);
       items = count * blocks_per_row;
       pairs = count > 1 ? count : 0;  // rows with one split write no partials
     }
-    scan[tid] = items;
-    pscan[tid] = pairs;
+    // inclusive scans of (items, pairs): within each warp by shuffles, then
+    // over the warp totals by warp 0
+    int a = items, b = pairs;
+#pragma unroll
+    for (int off = 1; off < 32; off <<= 1) {
+      const int ya = __shfl_up_sync(kFullMask, a, off);
+      const int yb = __shfl_up_sync(kFullMask, b, off);
+      if (lane >= off) {
+        a += ya;
+        b += yb;
+      }
+    }
+    if (lane == 31) {
+      wsum[warp] = a;
+      wpsum[warp] = b;
+    }
     __syncthreads();
-    for (int off = 1; off < kScheduleThreads; off <<= 1) {  // inclusive scans
-      const int add = tid >= off ? scan[tid - off] : 0;
-      const int padd = tid >= off ? pscan[tid - off] : 0;
-      __syncthreads();
-      scan[tid] += add;
-      pscan[tid] += padd;
-      __syncthreads();
+    if (warp == 0) {
+      int x = lane < kScheduleWarps ? wsum[lane] : 0;
+      int y = lane < kScheduleWarps ? wpsum[lane] : 0;
+#pragma unroll
+      for (int off = 1; off < 32; off <<= 1) {
+        const int ux = __shfl_up_sync(kFullMask, x, off);
+        const int uy = __shfl_up_sync(kFullMask, y, off);
+        if (lane >= off) {
+          x += ux;
+          y += uy;
+        }
+      }
+      if (lane < kScheduleWarps) {
+        wsum[lane] = x;
+        wpsum[lane] = y;
+      }
+    }
+    __syncthreads();
+    if (warp > 0) {
+      a += wsum[warp - 1];
+      b += wpsum[warp - 1];
     }
     if (q < p.rows) {
-      schedule[q] = carry + scan[tid] - items;
-      part_base[r] = pcarry + pscan[tid] - pairs;
+      schedule[q] = carry + a - items;
+      part_base[r] = pcarry + b - pairs;
     }
-    carry += scan[kScheduleThreads - 1];
-    pcarry += pscan[kScheduleThreads - 1];
-    __syncthreads();
+    carry += wsum[kScheduleWarps - 1];
+    pcarry += wpsum[kScheduleWarps - 1];
+    __syncthreads();  // the warp totals are rewritten by the next rows
   }
   if (tid == 0) {
     schedule[p.rows] = carry;
