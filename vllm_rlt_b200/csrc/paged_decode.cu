@@ -171,11 +171,17 @@ __device__ __forceinline__ void merge_splits(const DecodeParams& p, int row, int
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(kFullMask, mx, o));
   const float mref = mx == -INFINITY ? 0.f : mx;
+  // each split's weight 2^(m - mref) once, for the whole warp to read below
+  __shared__ float weights[kDecodeWarps][kMaxSplits];
+  float* w_of = weights[threadIdx.x >> 5];
   float total = 0.f;
   for (int sp = lane; sp < count; sp += 32) {
     const float2 ml = *reinterpret_cast<const float2*>(p.ws_ml + at(sp) * 2);
-    total += ml.y * ex2(ml.x - mref);
+    const float w = ex2(ml.x - mref);
+    w_of[sp] = w;
+    total += ml.y * w;
   }
+  __syncwarp();
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) total += __shfl_xor_sync(kFullMask, total, o);
   const float inv = 1.f / fmaxf(total, 1e-30f);
@@ -184,10 +190,14 @@ __device__ __forceinline__ void merge_splits(const DecodeParams& p, int row, int
   T* out = static_cast<T*>(p.out) + row * p.o_rs + qh * p.o_hs;
   for (int d4 = lane; d4 < p.head_dim / 4; d4 += 32) {
     float4 a = make_float4(0.f, 0.f, 0.f, 0.f);
+    // splits in order (the sum is the same as one split at a time); unrolled
+    // so several partial loads are in flight: a row split 128 ways is merged
+    // at the end of the call, on its critical path
     auto accumulate = [&](int64_t base, int s0, int s1) {
+#pragma unroll 4
       for (int sp = s0; sp < s1; ++sp) {
         const int64_t r = base + sp * stride;
-        const float w = ex2(p.ws_ml[r * 2] - mref);
+        const float w = w_of[sp];
         const float4 v = *reinterpret_cast<const float4*>(p.ws_o + r * p.head_dim + d4 * 4);
         a.x = fmaf(v.x, w, a.x);
         a.y = fmaf(v.y, w, a.y);
