@@ -118,14 +118,14 @@ def test_each_tensor_core_kernel_vs_oracle(dtype, page):
     split over two warps by key-column half; 5: as 3 with the softmax
     warpgroups' registers raised so a row's scores stay in registers for one
     pass; 6: as 5 with bf16 P split into hi + lo in query tiles whose rows
-    attend fewer than 512 keys; 7: as 6 in every tile) on long chunks that
-    run many key tiles, with ragged tails and a chunk shorter than one tile.
-    Kernels 2 and 3 differ only in where P is held, so their outputs are
-    bit-identical."""
+    attend fewer than 512 keys; 7: as 6 in every tile; 8: as 6 with 64-key
+    steps and two S buffers per query tile) on long chunks that run many key
+    tiles, with ragged tails and a chunk shorter than one tile. Kernels 2 and
+    3 differ only in where P is held, so their outputs are bit-identical."""
     case = dict(page=page, seed=11, prompt=(1500, 2100, 90, 777), prefix=(0, 700, 30, 1),
                 chunk_cap=1100)
     outs = {}
-    for version in (1, 2, 3, 4, 5, 6, 7):
+    for version in (1, 2, 3, 4, 5, 6, 7, 8):
         out, expected = _with_version(version, lambda: _prefix_reuse_case(dtype, **case))
         if version in ROUNDED_P_VERSIONS:
             assert_close(to_numpy(out), expected, dtype, **FA4_TOLERANCE[dtype])
@@ -180,7 +180,7 @@ def test_prefill_batch_invariance_bit_identical_sequences(dtype, d, group):
 
 
 @pytest.mark.parametrize("dtype", ["bf16", "f16"])
-@pytest.mark.parametrize("version", [1, 5, 6])
+@pytest.mark.parametrize("version", [1, 5, 6, 8])
 def test_pool_garbage_past_the_context_never_reaches_the_output(dtype, version):
     """Pages are copied whole, so the last context page's slots past the
     context come along; a pool allocated without initialisation may hold NaN

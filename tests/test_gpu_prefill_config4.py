@@ -100,10 +100,11 @@ def case():
     return config4_case()
 
 
-@pytest.mark.parametrize("version", [0, 5, 7])
+@pytest.mark.parametrize("version", [0, 5, 7, 8])
 def test_config4_prefill_matches_oracle_on_sampled_rows(case, version):
     """version 0: the library's default kernel; 5: P rounded to bf16; 7: P
-    split into a bf16 hi + lo pair everywhere."""
+    split into a bf16 hi + lo pair everywhere; 8: 64-key steps with two S
+    buffers per query tile."""
     lib = _lib.load()
     previous = lib.rlt_prefill_tc_select(version) if version else None
     try:

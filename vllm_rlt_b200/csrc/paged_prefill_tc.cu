@@ -1263,53 +1263,560 @@ __device__ __forceinline__ void pair_body(const PrefillTcParams& p) {
   }
 }
 
+// Whether this CTA's query tile A sees fewer than p.split_keys keys (its
+// rows then split P). Every warp finds the CTA's tile by itself, as
+// find_tile does (warp shuffles only), so the choice needs no shared memory
+// and no barrier.
+__device__ __forceinline__ bool cta_needs_split(const PrefillTcParams& p) {
+  const int lane = threadIdx.x & 31;
+  int running = 0, seq = -1, m0 = 0;
+  for (int base = 0; base < p.num_seqs && seq < 0; base += 32) {  // as find_tile
+    const int sq = base + lane;
+    int tiles = 0;
+    if (sq < p.num_seqs) {
+      const int qlen = p.cu[sq + 1] - p.cu[sq];
+      tiles = qlen > 0 ? (qlen + kPairRows - 1) / kPairRows : 0;
+    }
+    int incl = tiles;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int y = __shfl_up_sync(kFullMask, incl, o);
+      if (lane >= o) incl += y;
+    }
+    const int excl = running + incl - tiles;
+    const int target = static_cast<int>(blockIdx.x);
+    const bool mine = sq < p.num_seqs && target >= excl && target < excl + tiles;
+    const unsigned hit = __ballot_sync(kFullMask, mine);
+    if (hit) {
+      const int src = __ffs(hit) - 1;
+      seq = __shfl_sync(kFullMask, sq, src);
+      const int idx = __shfl_sync(kFullMask, tiles - 1 - (target - excl), src);  // heavy first
+      m0 = idx * kPairRows;
+    }
+    running += __shfl_sync(kFullMask, incl, 31);
+  }
+  if (seq < 0) return false;
+  const int qlen = p.cu[seq + 1] - p.cu[seq];
+  return p.lengths[seq] - qlen + m0 + 1 < p.split_keys;
+}
+
 // The kernel: CTAs whose query tile A sees fewer than p.split_keys keys (tile
 // B sees more) run the body that can split P; all others run the body
 // compiled without it, so the common path carries none of the split's
-// registers or branches. Every warp finds its CTA's tile by itself (warp
-// shuffles only), so the choice needs no shared memory and no barrier.
+// registers or branches.
 template <typename T, bool kPTmem, int kHalves, bool kWide, bool kSplitP = false>
 __global__ void __launch_bounds__(pair_threads(kHalves, kWide), 1)
     paged_prefill_tc2_kernel(const __grid_constant__ PrefillTcParams p) {
   if constexpr (kSplitP) {
-    const int lane = threadIdx.x & 31;
-    int running = 0, seq = -1, m0 = 0;
-    for (int base = 0; base < p.num_seqs && seq < 0; base += 32) {  // as find_tile
-      const int sq = base + lane;
-      int tiles = 0;
-      if (sq < p.num_seqs) {
-        const int qlen = p.cu[sq + 1] - p.cu[sq];
-        tiles = qlen > 0 ? (qlen + kPairRows - 1) / kPairRows : 0;
-      }
-      int incl = tiles;
-#pragma unroll
-      for (int o = 1; o < 32; o <<= 1) {
-        const int y = __shfl_up_sync(kFullMask, incl, o);
-        if (lane >= o) incl += y;
-      }
-      const int excl = running + incl - tiles;
-      const int target = static_cast<int>(blockIdx.x);
-      const bool mine = sq < p.num_seqs && target >= excl && target < excl + tiles;
-      const unsigned hit = __ballot_sync(kFullMask, mine);
-      if (hit) {
-        const int src = __ffs(hit) - 1;
-        seq = __shfl_sync(kFullMask, sq, src);
-        const int idx = __shfl_sync(kFullMask, tiles - 1 - (target - excl), src);  // heavy first
-        m0 = idx * kPairRows;
-      }
-      running += __shfl_sync(kFullMask, incl, 31);
-    }
-    bool split = false;
-    if (seq >= 0) {
-      const int qlen = p.cu[seq + 1] - p.cu[seq];
-      split = p.lengths[seq] - qlen + m0 + 1 < p.split_keys;
-    }
-    if (split) {
+    if (cta_needs_split(p)) {
       pair_body<T, kPTmem, kHalves, kWide, true>(p);
       return;
     }
   }
   pair_body<T, kPTmem, kHalves, kWide, false>(p);
+}
+
+// ---- version 8: 64-key steps, two S buffers per query tile ----------------
+//
+// The two-tile kernel above chains, per query tile and 128-key step: S ready
+// -> softmax -> P -> PV and the next S (16 MMAs) -> S ready, because P lives
+// in S's TMEM columns and TMEM (2 x S + 2 x O = 512 columns) has no room for
+// a second S. With 64-key steps an S tile is 64 columns, so each query tile
+// keeps two S buffers in the same 512 columns (S_A0, S_A1, S_B0, S_B1 in
+// [0, 256), O_A and O_B in [256, 512)): the MMA thread issues S_x(t+2) into
+// buffer t % 2 right after PV_x(t) has read P_x(t) from it, so S_x(t+1) is
+// already computed while the softmax of step t runs and the MMA latency and
+// the two hand-offs leave the per-step chain. P_x(t) (and with the split its
+// P_lo) overwrite the first 32 (64) columns of their S buffer. A rescale of
+// O_x (the lazy base moved) waits for PV_x(t-1) on bar_pv, which the MMA
+// thread now commits after every PV (S_x(t) no longer follows PV_x(t-1)).
+// K and V of a step are 16 KiB items in a 10-slot ring, consumed in the MMA
+// order K(0), K(1), then V(t), K(t+2) for t = 0, 1, ...
+//
+// Measured on the configs[3] workload: 749-788 TFLOP/s against 898-920 for
+// version 6 (~2,900 cycles per 64-key step against ~1,850 per 64 keys). With
+// N = 64 the S product re-reads the Q tile from shared memory twice as often
+// per key: a step moves ~128 KB of MMA operands plus 32 KB of TMA writes
+// through shared memory for 1,024 cycles of tensor work, more than its
+// 128 B/clock, so the hand-offs this version removes were not the whole
+// limit. It stays selectable (rlt_prefill_tc_select(8)) and parity-tested.
+constexpr int kKeys8 = 64;                              // keys per step
+constexpr int kItemBytes8 = kKeys8 * kHeadDim * 2;      // K or V of one step: 16 KiB
+constexpr int kItemHalf8 = kKeys8 * 128;                // 64 keys x 64 dims: 8 KiB
+constexpr int kRingSlots8 = 10;
+struct Pair8Shared {
+  uint64_t bar_q, bar_full[kRingSlots8], bar_empty[kRingSlots8];
+  // per (query tile x, S buffer b) at 2 x + b: S ready, and P written. P
+  // has one barrier per buffer because a tile's softmax may finish P_x(t+1)
+  // before the MMA thread has polled P_x(t): one barrier would then complete
+  // two phases before the poll and its parity would read as not done.
+  uint64_t bar_s[4], bar_p[4];
+  uint64_t bar_pv[2];
+  uint32_t tmem_base;
+  int tile_seq, tile_m0, abort_flag;
+};
+constexpr int kPair8Region = 2 * kTileBytes + kRingSlots8 * kItemBytes8;  // Q_A, Q_B, ring
+constexpr int kPair8Slack = kMaxSmem - kPair8Region - static_cast<int>(sizeof(Pair8Shared));
+static_assert(kPair8Slack >= 0, "shared memory per CTA (version 8)");
+
+__device__ __forceinline__ bool page_fits_step8(int page) { return page > 0 && kKeys8 % page == 0 && page % 8 == 0; }
+
+template <typename T, bool kSplitP>
+__device__ __forceinline__ void pair8_body(const PrefillTcParams& p) {
+  constexpr int kMmaWarp = 8;
+  constexpr int kProducerWarp = 9;
+  extern __shared__ uint8_t smem_raw[];
+  const uintptr_t raw = reinterpret_cast<uintptr_t>(smem_raw);
+  const uintptr_t skip = ((raw + 1023) & ~static_cast<uintptr_t>(1023)) - raw;
+  if (skip > static_cast<uintptr_t>(kPair8Slack) || !page_fits_step8(p.page)) {  // uniform
+    if (threadIdx.x == 0) raise_status(p.status, kStatusLayout);
+    return;
+  }
+  uint8_t* smem = smem_raw + skip;
+  uint8_t* ring = smem + 2 * kTileBytes;
+  Pair8Shared& sh = *reinterpret_cast<Pair8Shared*>(smem + kPair8Region);
+  uint64_t& bar_q = sh.bar_q;
+  uint64_t* bar_full = sh.bar_full;
+  uint64_t* bar_empty = sh.bar_empty;
+  uint64_t* bar_s = sh.bar_s;
+  uint64_t* bar_p = sh.bar_p;
+  uint64_t* bar_pv = sh.bar_pv;
+
+  const int tid = threadIdx.x;
+  const int warp = tid >> 5;
+  const int lane = tid & 31;
+  const int head = blockIdx.y;
+  const int kvh = head / p.group;
+
+  if (warp == 0)
+    find_tile<kPairRows, true>(p.cu, p.num_seqs, blockIdx.x, lane, &sh.tile_seq, &sh.tile_m0);
+  if (tid == 0) {
+    tc::mbar_init(&bar_q, 1);
+    for (int i = 0; i < kRingSlots8; ++i) {
+      tc::mbar_init(&bar_full[i], 1);
+      tc::mbar_init(&bar_empty[i], 1);
+    }
+    for (int i = 0; i < 4; ++i) {
+      tc::mbar_init(&bar_s[i], 1);
+      tc::mbar_init(&bar_p[i], 4);  // one arrival per softmax warp of the tile
+    }
+    for (int x = 0; x < 2; ++x) tc::mbar_init(&bar_pv[x], 1);
+    tc::fence_mbar_init();
+    sh.abort_flag = 0;
+  }
+  __syncwarp();
+  if (warp == 0) tc::tmem_alloc(&sh.tmem_base, kPairTmemCols);  // warp-collective
+  tc::tc_fence_before();
+  __syncthreads();
+  tc::tc_fence_after();
+  const uint32_t tmem = sh.tmem_base;
+  volatile int* aborted = &sh.abort_flag;
+
+  int seq = sh.tile_seq;
+  const int m0 = sh.tile_m0;
+  int qbegin = 0, qlen = 0, ctx = 0, n_steps = 0;
+  if (seq >= 0) {
+    qbegin = p.cu[seq];
+    qlen = p.cu[seq + 1] - qbegin;
+    ctx = p.lengths[seq];
+    if (qbegin < 0 || qlen <= 0 || qbegin + qlen > p.num_tokens || ctx < 0 ||
+        static_cast<int64_t>(ctx) > static_cast<int64_t>(p.width) * p.page) {
+      if (tid == 0) raise_status(p.status, kStatusBadSequence);
+      seq = -1;
+    } else {
+      const int kmax = ctx - qlen + min(qlen - 1, m0 + kPairRows - 1);
+      n_steps = kmax >= 0 ? kmax / kKeys8 + 1 : 0;
+    }
+  }
+  const bool active = seq >= 0 && n_steps > 0;
+  // the MMA thread and the softmax warps decide a tile's split alike
+  [[maybe_unused]] bool split_tile[2] = {false, false};
+  if constexpr (kSplitP) {
+    for (int x = 0; x < 2; ++x) split_tile[x] = ctx - qlen + m0 + x * kTileM + 1 < p.split_keys;
+  }
+
+  auto producer_role = [&]() {
+    // Lane j < pages per step loads page j of an item. Block ids are read a
+    // step before their K copy and kept for the V copy two steps later.
+    const int ppt = kKeys8 / p.page;
+    auto raw_id = [&](int u) {  // INT32_MIN: not a page of the context
+      int id = INT32_MIN;
+      if (lane < ppt && u < n_steps && (u * ppt + lane) * p.page < ctx)
+        id = p.tables[seq * p.t_rs + u * ppt + lane];
+      return id;
+    };
+    auto block_of = [&](int id) {
+      int blk = static_cast<int>(p.num_blocks);  // out of range: zero fill
+      if (id != INT32_MIN) {
+        if (id >= 0 && id < p.num_blocks)
+          blk = id;
+        else
+          raise_status(p.status, kStatusBadBlock);
+      }
+      return blk;
+    };
+    if (lane == 0) {
+      tc::prefetch_tensormap(&p.qmap);
+      tc::prefetch_tensormap(&p.kmap);
+      tc::prefetch_tensormap(&p.vmap);
+      tc::mbar_expect_tx(&bar_q, 2 * kTileBytes);
+      for (int x = 0; x < 2; ++x)
+        for (int dh = 0; dh < 2; ++dh)
+          tc::tma_load_3d(smem + x * kTileBytes + dh * kHalfBytes, &p.qmap, &bar_q, dh * 64, head,
+                          qbegin + m0 + x * kTileM);
+    }
+    int issued = 0;
+    bool stop = false;
+    auto emit = [&](bool is_v, int blk) {  // the next ring item
+      const int slot = issued % kRingSlots8;
+      int ok = 1;
+      if (lane == 0)
+        ok = *aborted == 0 &&
+             (issued < kRingSlots8 ||
+              tc::mbar_wait(&bar_empty[slot], (issued / kRingSlots8 - 1) & 1, kWaitLimit));
+      if (!__shfl_sync(kFullMask, ok, 0)) {
+        stop = true;
+        return;
+      }
+      uint8_t* dst = ring + slot * kItemBytes8;
+      const CUtensorMap* map = is_v ? &p.vmap : &p.kmap;
+      if (lane == 0) tc::mbar_expect_tx(&bar_full[slot], kItemBytes8);
+      __syncwarp();
+      if (lane < ppt) {
+#pragma unroll
+        for (int dh = 0; dh < 2; ++dh)
+          tc::tma_load_4d(dst + dh * kItemHalf8 + lane * p.page * 128, map, &bar_full[slot],
+                          dh * 64, kvh, 0, blk);
+      }
+      ++issued;
+    };
+    int f0 = block_of(raw_id(0));  // blocks of the steps whose K is out and V is not
+    int f1 = 0;
+    int pending = raw_id(1);
+    emit(false, f0);
+    if (!stop && n_steps > 1) {
+      f1 = block_of(pending);
+      pending = raw_id(2);
+      emit(false, f1);
+    }
+    for (int t = 0; !stop && t < n_steps; ++t) {
+      emit(true, f0);
+      f0 = f1;
+      if (!stop && t + 2 < n_steps) {
+        f1 = block_of(pending);
+        pending = raw_id(t + 3);
+        emit(false, f1);
+      }
+    }
+    if (lane == 0 && (stop || *aborted)) {  // let issued copies land before shared memory goes
+      *aborted = 1;
+      for (int i = issued - kRingSlots8 < 0 ? 0 : issued - kRingSlots8; i < issued; ++i)
+        tc::mbar_wait(&bar_full[i % kRingSlots8], (i / kRingSlots8) & 1, kWaitLimit);
+      tc::mbar_wait(&bar_q, 0, kWaitLimit);
+    }
+  };
+
+  auto mma_role = [&]() {
+    if (lane != 0) return;
+    constexpr uint32_t idesc_qk = tc::idesc_f16(Fmt<T>::value, kTileM, kKeys8, 0);
+    constexpr uint32_t idesc_pv = tc::idesc_f16(Fmt<T>::value, kTileM, kHeadDim, 1);
+    const uint64_t q_desc = tc::smem_desc_sw128(tc::smem_u32(smem), 16, 1024);
+    const uint64_t k_desc = tc::smem_desc_sw128(tc::smem_u32(ring), 16, 1024);
+    const uint64_t v_desc = tc::smem_desc_sw128(tc::smem_u32(ring), kItemHalf8, 1024);
+    const uint32_t q_lo = static_cast<uint32_t>(q_desc), q_hi = static_cast<uint32_t>(q_desc >> 32);
+    const uint32_t k_lo = static_cast<uint32_t>(k_desc), k_hi = static_cast<uint32_t>(k_desc >> 32);
+    const uint32_t v_lo = static_cast<uint32_t>(v_desc), v_hi = static_cast<uint32_t>(v_desc >> 32);
+    int commits_s[4] = {0, 0, 0, 0}, commits_pv[2] = {0, 0};
+    auto wait_item = [&](int i) {
+      return tc::mbar_wait(&bar_full[i % kRingSlots8], (i / kRingSlots8) & 1, kWaitLimit);
+    };
+    // S_x into buffer b = Q_x K^T (M 128, N 64 keys, K 128 dims), K in slot `slot`
+    auto s_mma = [&](int x, int b, int slot) {
+      const uint32_t qb = q_lo + x * (kTileBytes >> 4);
+      const uint32_t kb = k_lo + slot * (kItemBytes8 >> 4);
+#pragma unroll
+      for (int ks = 0; ks < 8; ++ks) {
+        const uint32_t q_off = ((ks >> 2) * kHalfBytes + (ks & 3) * 32) >> 4;
+        const uint32_t k_off = ((ks >> 2) * kItemHalf8 + (ks & 3) * 32) >> 4;
+        tc::mma_f16_ss(tmem + x * 128 + b * kKeys8, tc::desc64(qb + q_off, q_hi),
+                       tc::desc64(kb + k_off, k_hi), idesc_qk, ks > 0 ? 1u : 0u);
+      }
+      tc::mma_commit(&bar_s[2 * x + b]);
+      ++commits_s[2 * x + b];
+    };
+    // O_x += P_x V over the step's 64 keys (P in buffer b's first columns)
+    auto pv_mma = [&](int x, int b, int slot, uint32_t accumulate) {
+      const uint32_t vb = v_lo + slot * (kItemBytes8 >> 4);
+      const uint32_t p_col = tmem + x * 128 + b * kKeys8;
+#pragma unroll
+      for (int ks = 0; ks < 4; ++ks)
+        tc::mma_f16_ts(tmem + 256 + x * kHeadDim, p_col + ks * 8,
+                       tc::desc64(vb + ks * (2048 >> 4), v_hi), idesc_pv, ks > 0 ? 1u : accumulate);
+      if constexpr (kSplitP) {
+        if (split_tile[x]) {
+#pragma unroll
+          for (int ks = 0; ks < 4; ++ks)
+            tc::mma_f16_ts(tmem + 256 + x * kHeadDim, p_col + 32 + ks * 8,
+                           tc::desc64(vb + ks * (2048 >> 4), v_hi), idesc_pv, 1u);
+        }
+      }
+      tc::mma_commit(&bar_pv[x]);
+      ++commits_pv[x];
+    };
+    bool ok = tc::mbar_wait(&bar_q, 0, kWaitLimit) && wait_item(0);
+    int item = 0;
+    if (ok) {
+      tc::tc_fence_after();
+      s_mma(0, 0, 0);
+      s_mma(1, 0, 0);
+      tc::mma_commit(&bar_empty[0]);  // K(0) read by both S MMAs
+      item = 1;
+      if (n_steps > 1) {
+        ok = wait_item(1);
+        if (ok) {
+          tc::tc_fence_after();
+          s_mma(0, 1, 1 % kRingSlots8);
+          s_mma(1, 1, 1 % kRingSlots8);
+          tc::mma_commit(&bar_empty[1 % kRingSlots8]);
+          item = 2;
+        }
+      }
+    }
+    for (int t = 0; ok && t < n_steps; ++t) {
+      const int b = t & 1;
+      const int v_item = item++;
+      const int v_slot = v_item % kRingSlots8;
+      const bool more = t + 2 < n_steps;
+      const int k_item = more ? item++ : -1;
+      const int k_slot = more ? k_item % kRingSlots8 : 0;
+      ok = wait_item(v_item) && (!more || wait_item(k_item));
+      if (ok && t == n_steps - 1) {
+        // V rows past the context of its last page may hold any bits (NaN
+        // included) and P is 0 there: zero them so P V stays finite
+        uint8_t* vt = ring + v_slot * kItemBytes8;
+        const int r0 = ctx - t * kKeys8;
+        const int page_end = (ctx + p.page - 1) / p.page * p.page;
+        const int r1 = min(kKeys8, page_end - t * kKeys8);
+        for (int r = max(r0, 0); r < r1; ++r)
+#pragma unroll
+          for (int half = 0; half < 2; ++half)
+#pragma unroll
+            for (int c = 0; c < 8; ++c)
+              *reinterpret_cast<uint4*>(vt + half * kItemHalf8 + r * 128 + c * 16) =
+                  make_uint4(0, 0, 0, 0);
+        tc::fence_proxy_async_smem();
+      }
+      for (int x = 0; ok && x < 2; ++x) {
+        ok = tc::mbar_poll(&bar_p[2 * x + b], (t >> 1) & 1, kWaitLimit);
+        if (!ok) break;
+        tc::tc_fence_after();
+        pv_mma(x, b, v_slot, t > 0 ? 1u : 0u);
+        if (more) s_mma(x, b, k_slot);  // S_x(t+2) into the buffer PV_x(t) just read
+      }
+      if (!ok) break;
+      tc::mma_commit(&bar_empty[v_slot]);  // V(t) read by both PV MMAs
+      if (more) tc::mma_commit(&bar_empty[k_slot]);  // K(t+2) read by both S MMAs
+    }
+    if (!ok) {
+      *aborted = 1;
+      // every commit arrives once all earlier MMAs are done: wait for the
+      // last two phases of each barrier in order
+      auto drain = [&](uint64_t* bar, int commits) {
+        if (commits > 1) tc::mbar_wait(bar, (commits - 2) & 1, kWaitLimit);
+        if (commits > 0) tc::mbar_wait(bar, (commits - 1) & 1, kWaitLimit);
+      };
+      for (int x = 0; x < 2; ++x) drain(&bar_pv[x], commits_pv[x]);
+      for (int i = 0; i < 4; ++i) drain(&bar_s[i], commits_s[i]);
+    }
+  };
+
+  auto softmax_role = [&]() {
+    const int x = warp >> 2;
+    const int quarter = warp & 3;  // TMEM lanes [32 quarter, 32 quarter + 32)
+    const int r = quarter * 32 + lane;
+    const uint32_t lane_base = static_cast<uint32_t>(quarter * 32) << 16;
+    const uint32_t o_tmem = tmem + 256 + x * kHeadDim + lane_base;
+    const int qi = m0 + x * kTileM + r;
+    const int row_limit = min(ctx - qlen + qi, ctx - 1);
+    float m_used = -INFINITY;
+    float l_sum = 0.f;
+    int t = 0;
+    for (; t < n_steps; ++t) {
+      const int b = t & 1;
+      const bool ready = __all_sync(
+          kFullMask, *aborted == 0 && tc::mbar_wait(&bar_s[2 * x + b], (t >> 1) & 1, kWaitLimit));
+      if (!ready) {
+        *aborted = 1;
+        break;
+      }
+      tc::tc_fence_after();
+      const uint32_t s_tmem = tmem + x * 128 + b * kKeys8 + lane_base;
+      const int n0 = t * kKeys8;
+      const bool diagonal = __any_sync(kFullMask, n0 + kKeys8 - 1 > row_limit);
+      uint32_t sr[2][32];
+      tc::tmem_ld32(s_tmem, sr[0]);
+      tc::tmem_ld32(s_tmem + 32, sr[1]);
+      tc::tmem_ld_wait(sr[0]);
+      tc::tmem_ld_wait(sr[1]);
+      if (diagonal) {
+#pragma unroll
+        for (int c = 0; c < 2; ++c)
+#pragma unroll
+          for (int j = 0; j < 32; ++j)
+            if (n0 + c * 32 + j > row_limit) sr[c][j] = __float_as_uint(-INFINITY);
+      }
+      float mc[2];
+#pragma unroll
+      for (int c = 0; c < 2; ++c) {
+        mc[c] = -INFINITY;
+#pragma unroll
+        for (int j = 0; j < 32; j += 2)
+          mc[c] = max3(mc[c], __uint_as_float(sr[c][j]), __uint_as_float(sr[c][j + 1]));
+      }
+      const float m_new = fmaxf(m_used, fmaxf(mc[0], mc[1]) * p.scale_log2);
+      float factor = 1.f;
+      if (m_new > m_used + 8.f) {
+        factor = ex2(m_used - m_new);
+        m_used = m_new;
+      }
+      const float neg_mref = m_used == -INFINITY ? 0.f : -m_used;
+      if (t > 0 && __any_sync(kFullMask, factor != 1.f)) {
+        // O_x is quiescent once PV_x(t-1) is done. S_x(t) ready implies
+        // PV_x(t-2) done (S_x(t) followed it into the same buffer), so the
+        // barrier is in phase t-1 or past it and one parity wait is exact.
+        if (!__all_sync(kFullMask, tc::mbar_wait(&bar_pv[x], (t - 1) & 1, kWaitLimit))) {
+          *aborted = 1;
+          break;
+        }
+        tc::tc_fence_after();
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+          uint32_t o[32];
+          tc::tmem_ld32(o_tmem + c * 32, o);
+          tc::tmem_ld_wait(o);
+#pragma unroll
+          for (int j = 0; j < 32; ++j) o[j] = __float_as_uint(__uint_as_float(o[j]) * factor);
+          tc::tmem_st32(o_tmem + c * 32, o);
+        }
+        tc::tmem_st_wait();
+      }
+      const uint64_t scale2 = pk2(p.scale_log2, p.scale_log2);
+      const uint64_t neg2 = pk2(neg_mref, neg_mref);
+      auto emit_p = [&](auto split) {
+        constexpr bool kSplit = decltype(split)::value;
+        uint64_t psum2 = pk2(0.f, 0.f);
+#pragma unroll
+        for (int c = 0; c < 2; ++c) {
+          uint32_t packed[16];
+          [[maybe_unused]] uint32_t rest[16];  // P_lo
+#pragma unroll
+          for (int j = 0; j < 32; j += 2) {
+            const uint64_t arg =
+                fma2(pk2(__uint_as_float(sr[c][j]), __uint_as_float(sr[c][j + 1])), scale2, neg2);
+            float p0, p1;
+            upk2(arg, p0, p1);
+            p0 = ex2(p0);
+            p1 = ex2(p1);
+            psum2 = add2(psum2, pk2(p0, p1));
+            packed[j / 2] = pack2<T>(p0, p1);
+            if constexpr (kSplit) {
+              float h0, h1;
+              unpack2<T>(packed[j / 2], h0, h1);
+              rest[j / 2] = pack2<T>(p0 - h0, p1 - h1);
+            }
+          }
+          tc::tmem_st16(s_tmem + c * 16, packed);  // S columns already in registers
+          if constexpr (kSplit) tc::tmem_st16(s_tmem + 32 + c * 16, rest);
+        }
+        return psum2;
+      };
+      uint64_t psum2;
+      if (kSplitP && split_tile[x])
+        psum2 = emit_p(std::integral_constant<bool, kSplitP>{});
+      else
+        psum2 = emit_p(std::false_type{});
+      float lo, hi;
+      upk2(psum2, lo, hi);
+      l_sum = l_sum * factor + (lo + hi);
+      tc::tmem_st_wait();
+      tc::tc_fence_before();
+      __syncwarp();  // every lane's P is written before the warp's single arrival
+      if (lane == 0) tc::mbar_arrive(&bar_p[2 * x + b]);
+    }
+    if (t == n_steps) {
+      // S_x(n-1) ready implied PV_x(n-3) done, so PV_x(n-2) and PV_x(n-1) may
+      // both be pending: wait for their phases in order (one wait on the last
+      // parity alone would match the completed phase n-3)
+      bool done = n_steps < 2 || tc::mbar_wait(&bar_pv[x], (n_steps - 2) & 1, kWaitLimit);
+      done = done && tc::mbar_wait(&bar_pv[x], (n_steps - 1) & 1, kWaitLimit);
+      if (!__all_sync(kFullMask, done)) *aborted = 1;
+      tc::tc_fence_after();
+    }
+    if (t == n_steps && !__any_sync(kFullMask, *aborted != 0)) {
+      const bool store = qi < qlen;
+      T* dst = static_cast<T*>(p.out) + (qbegin + (store ? qi : 0)) * p.o_rs + head * p.o_hs;
+      const float inv = l_sum > 0.f ? 1.f / l_sum : 0.f;
+#pragma unroll
+      for (int c = 0; c < kHeadDim / 32; ++c) {
+        uint32_t o[32];
+        tc::tmem_ld32(o_tmem + c * 32, o);
+        tc::tmem_ld_wait(o);
+        if (!store) continue;
+#pragma unroll
+        for (int v = 0; v < 4; ++v) {
+          uint4 w;
+          w.x = pack2<T>(__uint_as_float(o[v * 8 + 0]) * inv, __uint_as_float(o[v * 8 + 1]) * inv);
+          w.y = pack2<T>(__uint_as_float(o[v * 8 + 2]) * inv, __uint_as_float(o[v * 8 + 3]) * inv);
+          w.z = pack2<T>(__uint_as_float(o[v * 8 + 4]) * inv, __uint_as_float(o[v * 8 + 5]) * inv);
+          w.w = pack2<T>(__uint_as_float(o[v * 8 + 6]) * inv, __uint_as_float(o[v * 8 + 7]) * inv);
+          *reinterpret_cast<uint4*>(dst + c * 32 + v * 8) = w;
+        }
+      }
+    }
+  };
+  auto zero_rows = [&]() {
+    const int qi = m0 + (warp >> 2) * kTileM + (tid & (kTileM - 1));
+    if (qi < qlen) {
+      T* dst = static_cast<T*>(p.out) + (qbegin + qi) * p.o_rs + head * p.o_hs;
+      for (int c = 0; c < kHeadDim; c += 8) *reinterpret_cast<uint4*>(dst + c) = make_uint4(0, 0, 0, 0);
+    }
+  };
+  if (warp >= 8) {
+    tc::setmaxnreg_dec<kWideOtherRegs>();
+    if (active && warp == kProducerWarp)
+      producer_role();
+    else if (active && warp == kMmaWarp)
+      mma_role();
+  } else {
+    tc::setmaxnreg_inc<kWideSoftRegs>();
+    if (active)
+      softmax_role();
+    else if (seq >= 0 && n_steps == 0)
+      zero_rows();
+  }
+  __syncthreads();
+  if (*aborted && tid == 0) raise_status(p.status, kStatusTimeout);
+  tc::tc_fence_before();
+  __syncthreads();
+  if (warp == 0) {
+    tc::tc_fence_after();
+    tc::tmem_dealloc(tmem, kPairTmemCols);
+  }
+}
+
+// Version 8 kernel: the same per-CTA choice between the split and unsplit
+// bodies as version 6 (the split only where query tile A sees fewer than
+// p.split_keys keys).
+template <typename T, bool kSplitP>
+__global__ void __launch_bounds__(pair_threads(1, true), 1)
+    paged_prefill_tc8_kernel(const __grid_constant__ PrefillTcParams p) {
+  if constexpr (kSplitP) {
+    if (cta_needs_split(p)) {
+      pair8_body<T, true>(p);
+      return;
+    }
+  }
+  pair8_body<T, false>(p);
 }
 
 // ---- host side --------------------------------------------------------------
@@ -1346,14 +1853,35 @@ bool aligned16(const void* ptr) { return (reinterpret_cast<uintptr_t>(ptr) & 15u
 // with P split everywhere, 5 = warp-specialised two-tile kernel with P in
 // TMEM and register-resident scores, 4 = split softmax (two warps per row
 // set), 3 = one warp per row set reading S from TMEM twice, 2 = as 3 with P
-// in shared memory, 1 = the single-tile kernel. 6 costs no measurable time
-// over 5 on the configs[3] workload (CTAs without a splitting tile run a body
-// compiled without the split).
+// in shared memory, 1 = the single-tile kernel, 8 = 6 with 64-key steps and
+// two S buffers per query tile (pages of 8 to 64 tokens; 128-token pages run
+// 6). 6 costs no measurable time over 5 on the configs[3] workload (CTAs
+// without a splitting tile run a body compiled without the split).
 std::atomic<int> g_prefill_version{6};
 // Version 6 splits P in query tiles whose first row sees fewer keys than
 // this; over more keys the bf16 roundings of P average out (error ~ 2^-9 x
 // 1.6 / sqrt(keys) per output at unit-variance scores, below 1e-4 here).
 constexpr int kSplitKeys = 512;
+
+template <typename T, bool kSplitP>
+cudaError_t launch_pair8(dim3 grid, const PrefillTcParams& p, cudaStream_t stream) {
+  auto kernel = paged_prefill_tc8_kernel<T, kSplitP>;
+  static std::once_flag once;
+  static cudaError_t attr_err = cudaSuccess;
+  std::call_once(once, [kernel] {
+    attr_err = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kMaxSmem);
+    if (attr_err == cudaSuccess) {
+      // the register split assumes this launch allocation (as launch_pair)
+      cudaFuncAttributes attr{};
+      attr_err = cudaFuncGetAttributes(&attr, kernel);
+      if (attr_err == cudaSuccess && attr.numRegs < kWideLaunchRegs)
+        attr_err = cudaErrorInvalidConfiguration;
+    }
+  });
+  if (attr_err != cudaSuccess) return attr_err;
+  kernel<<<grid, pair_threads(1, true), kMaxSmem, stream>>>(p);
+  return cudaSuccess;
+}
 
 template <typename T, bool kPTmem, int kHalves, bool kWide = false, bool kSplitP = false>
 cudaError_t launch_pair(dim3 grid, const PrefillTcParams& p, cudaStream_t stream) {
@@ -1496,7 +2024,10 @@ int paged_prefill_tc(const void* q, const void* key_cache, const void* value_cac
   else if (version == 5)
     err = dtype == RLT_BF16 ? launch_pair<__nv_bfloat16, true, 1, true>(grid, p, stream)
                             : launch_pair<__half, true, 1, true>(grid, p, stream);
-  else  // 6 / 7: bf16 splits P into hi + lo (fp16's 11-bit P needs no split)
+  else if (version == 8 && kKeys8 % page == 0)
+    err = dtype == RLT_BF16 ? launch_pair8<__nv_bfloat16, true>(grid, p, stream)
+                            : launch_pair8<__half, false>(grid, p, stream);
+  else  // 6 / 7 (and 8 with 128-token pages): bf16 splits P into hi + lo (fp16's 11-bit P needs no split)
     err = dtype == RLT_BF16 ? launch_pair<__nv_bfloat16, true, 1, true, true>(grid, p, stream)
                             : launch_pair<__half, true, 1, true>(grid, p, stream);
   if (err != cudaSuccess) return static_cast<int>(err);
@@ -1507,7 +2038,7 @@ int paged_prefill_tc(const void* q, const void* key_cache, const void* value_cac
 }  // namespace rlt
 
 extern "C" int rlt_prefill_tc_select(int32_t version) {
-  if (version < 1 || version > 7) return rlt::g_prefill_version.load();
+  if (version < 1 || version > 8) return rlt::g_prefill_version.load();
   return rlt::g_prefill_version.exchange(version);
 }
 
