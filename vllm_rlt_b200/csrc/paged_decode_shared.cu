@@ -6,13 +6,15 @@
 // tables at the same physical pages for a common prompt prefix. The plain
 // decode kernel reads those pages once per row. Here a host-built plan cuts
 // the work into chunks: a chunk is a token range of one table row together
-// with the rows (members) that share it. One CTA reads each 32-token sub-tile
-// of its chunk once and runs the online softmax of every (member row, query
-// head) pair of its KV head on it, writing an fp32 partial (o, max, sum) per
-// pair. Each row's own tokens after the shared prefix go through the plain
-// decode kernel first (rlt_paged_decode_lse on per-row suffix tables), which
-// leaves the suffix result in `out` and its log-sum-exp in `suffix_lse`; a
-// merge kernel then folds the prefix partials into `out`. Result = softmax(q K^T * scale) V over
+// with the rows (members) that share it. One CTA per (chunk, KV head) reads
+// each sub-tile of its chunk once (64 tokens on the 16-bit tensor-core path,
+// 32 in fp32) and runs the online softmax of every (member row, query head)
+// pair of its KV head on it, writing an fp32 partial (o, max, sum) per pair.
+// Each row's own tokens after the shared prefix go through the plain decode
+// kernel (rlt_paged_decode_lse on per-row suffix tables, on the caller's
+// stream beside the chunks), which leaves the suffix result in `out` and its
+// log-sum-exp in `suffix_lse`; a merge kernel then folds the prefix partials
+// into `out`. Result = softmax(q K^T * scale) V over
 // the row's context, the semantics of torch_paged_attention
 // (vllm_rlt/kernels/paged_attention.py:12-36).
 //

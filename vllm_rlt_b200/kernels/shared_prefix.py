@@ -11,6 +11,8 @@ like the reference's, reads such pages once per row. Here:
 * ``plan_shared_prefix`` turns each group's shared prefix into chunks -- a
   token range of the group's first table row plus the member rows that attend
   to it -- with one partial slot per (member, chunk), rows' slots contiguous;
+  the chunk length defaults to ``choose_chunk_tokens`` (the smallest whose
+  chunk CTAs fit one resident wave of the chunk kernel);
   and gives every row a suffix table (its own table shifted past its shared
   pages) and suffix length for the tokens only it reads;
 * ``paged_attention_shared`` runs the plain decode kernel on the suffix
