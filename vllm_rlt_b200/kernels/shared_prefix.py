@@ -15,17 +15,19 @@ like the reference's, reads such pages once per row. Here:
   chunk CTAs fit one resident wave of the chunk kernel);
   and gives every row a suffix table (its own table shifted past its shared
   pages) and suffix length for the tokens only it reads;
-* ``paged_attention_shared`` runs the plain decode kernel on the suffix
-  tables (``rlt_paged_decode_lse``: the suffix result lands in the output,
-  its log-sum-exp beside it), then ``rlt_paged_decode_shared``: each prefix
-  chunk's K/V is read once and attended by all its members, and the partials
-  are merged into the output.
+* ``paged_attention_shared`` derives each row's suffix table and length on
+  the device from the call's own tables and lengths
+  (``rlt_shared_prefix_suffix``), runs the prefix chunks on a side stream
+  (each chunk's K/V read once and attended by all its members) beside the
+  plain decode kernel on the suffix tables (``rlt_paged_decode_lse``: the
+  suffix result lands in the output, its log-sum-exp beside it), and merges
+  the chunk partials into the output after both.
 
 The result equals ``paged_attention`` on the same tables and lengths (fp32
 online softmax in a different order: within fp32 rounding). The plan is built
 on the host from host copies of the tables and lengths, once per batch
-layout; it is not meant for CUDA-graph capture across steps whose lengths
-change.
+layout; it stays valid while the rows grow, so a captured CUDA graph can
+replay the call step after step. Rebuild it when the batch's rows change.
 """
 
 from __future__ import annotations
