@@ -143,9 +143,12 @@ int rlt_paged_prefill(const void* q, const void* key_cache, const void* value_ca
  * wheel makes the same choice internally. */
 int rlt_paged_prefill_uses_tensor_cores(int32_t dtype, int32_t head_dim, int32_t page_size);
 
-/* Diagnostics: choose the tensor-core prefill kernel for the process (5 =
- * warp-specialised two-tile kernel with P in TMEM whose softmax warpgroups
- * hold a row's 128 scores in registers (setmaxnreg), the default; 4 = P in
+/* Diagnostics: choose the tensor-core prefill kernel for the process (6 =
+ * the default: 5 with bf16 P split into a hi + lo pair in the query tiles
+ * whose rows attend fewer than 512 keys; 7 = 5 with P split everywhere; 8 =
+ * 6 with 64-key steps and two S buffers per query tile (pages of 8 to 64
+ * tokens); 5 = warp-specialised two-tile kernel with P in TMEM whose softmax
+ * warpgroups hold a row's 128 scores in registers (setmaxnreg); 4 = P in
  * TMEM, each row's softmax split over two warps by key-column half; 3 = P in
  * TMEM, one warp per 32 rows reading S twice; 2 = as 3 with P in shared
  * memory; 1 = single-tile kernel); returns the previous choice (any other
