@@ -99,17 +99,24 @@ __global__ void __launch_bounds__(256) rms_norm_vec_kernel(
   __shared__ float partial[33];
   const int row = blockIdx.x;
   const int nvec = hidden / V;
+  // every input this thread needs is loaded up front (x, the weights, the
+  // residual), so the two reductions wait on one memory round trip, not three
+  uint4 xr[kNV], wr[kNV], rr[kNV], w2r[kNV];
+  const uint4 zero = make_uint4(0, 0, 0, 0);
+#pragma unroll
+  for (int k = 0; k < kNV; ++k) {
+    const int vi = threadIdx.x + k * blockDim.x;
+    const bool in = vi < nvec;
+    xr[k] = in ? ld_vec(x + row * x_stride + vi * V) : zero;
+    wr[k] = in ? ld_vec(w + vi * V) : zero;
+    rr[k] = in && residual != nullptr ? ld_vec(residual + row * r_stride + vi * V) : zero;
+    w2r[k] = in && w2 != nullptr ? ld_vec(w2 + vi * V) : zero;
+  }
   float vals[kNV][V];
   float ss = 0.f;
 #pragma unroll
   for (int k = 0; k < kNV; ++k) {
-    const int vi = threadIdx.x + k * blockDim.x;
-    if (vi < nvec) {
-      unpack16<T>(ld_vec(x + row * x_stride + vi * V), vals[k]);
-    } else {
-#pragma unroll
-      for (int e = 0; e < V; ++e) vals[k][e] = 0.f;
-    }
+    unpack16<T>(xr[k], vals[k]);
 #pragma unroll
     for (int e = 0; e < V; ++e) ss = fmaf(vals[k][e], vals[k][e], ss);
   }
@@ -120,10 +127,10 @@ __global__ void __launch_bounds__(256) rms_norm_vec_kernel(
     const int vi = threadIdx.x + k * blockDim.x;
     if (vi >= nvec) continue;
     float wv[V], y[V];
-    unpack16<T>(ld_vec(w + vi * V), wv);
+    unpack16<T>(wr[k], wv);
     if (residual != nullptr) {
       float rv[V];
-      unpack16<T>(ld_vec(residual + row * r_stride + vi * V), rv);
+      unpack16<T>(rr[k], rv);
 #pragma unroll
       for (int e = 0; e < V; ++e) y[e] = rnd<T>(add(rv[e], rnd<T>(mul(wv[e], rnd<T>(mul(vals[k][e], inv))))));
     } else {
@@ -144,7 +151,7 @@ __global__ void __launch_bounds__(256) rms_norm_vec_kernel(
     const int vi = threadIdx.x + k * blockDim.x;
     if (vi >= nvec) continue;
     float wv[V], y[V];
-    unpack16<T>(ld_vec(w2 + vi * V), wv);
+    unpack16<T>(w2r[k], wv);
 #pragma unroll
     for (int e = 0; e < V; ++e) y[e] = rnd<T>(mul(wv[e], rnd<T>(mul(vals[k][e], inv2))));
     st_vec(out2 + row * o2_stride + vi * V, pack16<T>(y));
