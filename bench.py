@@ -309,6 +309,63 @@ def single_thread_rate(plan, fn, budget_s=3.0):
         torch.set_num_threads(before)
 
 
+def prefill_cpu_baseline(budget_s=5.0, rows_per_seq=32, seqs=4):
+    """configs[3] on the host: the reference's CPU attention path
+    (torch_paged_attention, vllm_rlt/kernels/paged_attention.py:12-36) over
+    per-token query rows, each row attending its bottom-right causal context
+    (the flat-table form of tests/test_flash_attention.py:169-186). A seeded
+    sample: ``seqs`` prompts of the bench plan, ``rows_per_seq`` query rows of
+    each spread over its computed (not reused) tokens; TFLOP/s on the bench's
+    count (4 x D x Hq per attended key), repeated for about ``budget_s``
+    seconds on all host cores."""
+    import torch
+
+    from vllm_rlt_b200 import workloads
+
+    torch.set_num_threads(os.cpu_count() or 1)
+    fn, kind, label = reference_cpu_path()
+    plan = workloads.config4_plan(seed=100)
+    rng = np.random.default_rng(5)
+    picks = rng.choice(len(plan.prompt_lengths), size=seqs, replace=False)
+    g = torch.Generator().manual_seed(9)
+    page, hkv, d, hq = 16, 16, 128, 16
+    qs, ks, vs, tabs, lens, firsts = [], [], [], [], [], 0
+    for sq in picks:
+        length = int(plan.prompt_lengths[sq])
+        pages = -(-length // page)
+        ks.append(torch.randn((pages, page, hkv, d), generator=g).to(torch.bfloat16))
+        vs.append(torch.randn((pages, page, hkv, d), generator=g).to(torch.bfloat16))
+        start = int(plan.reused[sq])  # reused prefix rows are not queries
+        rows = np.unique(np.linspace(start, length - 1, rows_per_seq).astype(np.int64))
+        for r in rows:
+            t = np.full(-(-length // page), -1, dtype=np.int32)
+            t[:pages] = np.arange(firsts, firsts + pages, dtype=np.int32)
+            tabs.append(t)
+            lens.append(int(r) + 1)  # query token r of the prompt sees keys 0..r
+        firsts += pages
+        qs.append(torch.randn((len(rows), hq, d), generator=g).to(torch.bfloat16))
+    width = max(len(t) for t in tabs)
+    tables = np.full((len(tabs), width), -1, dtype=np.int32)
+    for i, t in enumerate(tabs):
+        tables[i, : len(t)] = t
+    q = torch.cat(qs)
+    key, value = torch.cat(ks), torch.cat(vs)
+    t_tables = torch.from_numpy(tables)
+    t_lengths = torch.tensor(lens, dtype=torch.int32)
+    flops = 4 * d * hq * int(sum(lens))
+    fn(q, key, value, t_tables, t_lengths)
+    reps, spent = 0, 0.0
+    while spent < budget_s and reps < 20:
+        t0 = time.perf_counter()
+        fn(q, key, value, t_tables, t_lengths)
+        spent += time.perf_counter() - t0
+        reps += 1
+    return {"value": round(flops * reps / spent / 1e12, 5), "unit": "TFLOP/s", "kind": kind,
+            "cores": torch.get_num_threads(),
+            "sample": f"{len(lens)} query rows of {seqs} configs[3] prompts (sum of attended "
+                      f"keys {int(sum(lens))}) x {reps} calls; {label}"}
+
+
 def reference_kv_cpu(batch=64, reps=20):
     """BASELINE B4: the reference's CPU KVCacheManager.write (one layer, a
     batch of rows) and finalize_token (one token, every layer, into the deeper
@@ -1200,6 +1257,11 @@ def run_ours(args):
             except Exception as error:  # reported, never silently dropped
                 extras[name] = {"error": f"{type(error).__name__}: {error}"}
             torch.cuda.empty_cache()
+        if rank == 0 and world == 1 and not args.no_cpu_baseline and "value" in extras["prefill"]:
+            try:  # the reference's CPU path on a sample of the prefill workload
+                extras["prefill"]["cpu_baseline"] = prefill_cpu_baseline()
+            except Exception as error:
+                extras["prefill"]["cpu_baseline"] = {"error": f"{type(error).__name__}: {error}"}
 
     if world > 1:
         dist.barrier(device_ids=[local])
