@@ -366,6 +366,26 @@ def prefill_cpu_baseline(budget_s=5.0, rows_per_seq=32, seqs=4):
                       f"keys {int(sum(lens))}) x {reps} calls; {label}"}
 
 
+def longctx_cpu_baseline(budget_s=5.0):
+    """configs[4] on the host: the reference's CPU decode path on a seeded row
+    sample of the one-GPU request set (as the decode line's cpu_baseline)."""
+    from vllm_rlt_b200 import workloads
+
+    plan = workloads.config5_plan(seed=0, rows=64)
+    host, fn, kind, label, threads = reference_cpu_sample(plan, budget_s / 2)
+    host.run(fn)
+    reps, spent = 0, 0.0
+    while spent < budget_s and reps < 20:
+        t0 = time.perf_counter()
+        host.run(fn)
+        spent += time.perf_counter() - t0
+        reps += 1
+    return {"value": round(host.bytes * reps / spent / 1e9, 3), "unit": "GB/s", "kind": kind,
+            "cores": threads,
+            "sample": f"{len(host.rows)} of {plan.num_rows} rows (sum ctx {host.tokens}) x "
+                      f"{reps} calls; {label}"}
+
+
 def reference_kv_cpu(batch=64, reps=20):
     """BASELINE B4: the reference's CPU KVCacheManager.write (one layer, a
     batch of rows) and finalize_token (one token, every layer, into the deeper
@@ -1257,11 +1277,15 @@ def run_ours(args):
             except Exception as error:  # reported, never silently dropped
                 extras[name] = {"error": f"{type(error).__name__}: {error}"}
             torch.cuda.empty_cache()
-        if rank == 0 and world == 1 and not args.no_cpu_baseline and "value" in extras["prefill"]:
-            try:  # the reference's CPU path on a sample of the prefill workload
-                extras["prefill"]["cpu_baseline"] = prefill_cpu_baseline()
-            except Exception as error:
-                extras["prefill"]["cpu_baseline"] = {"error": f"{type(error).__name__}: {error}"}
+        if rank == 0 and world == 1 and not args.no_cpu_baseline:
+            # the reference's CPU path on samples of the prefill and long-context workloads
+            for name, fn in (("prefill", prefill_cpu_baseline), ("longctx", longctx_cpu_baseline)):
+                if "value" not in extras[name]:
+                    continue
+                try:
+                    extras[name]["cpu_baseline"] = fn()
+                except Exception as error:
+                    extras[name]["cpu_baseline"] = {"error": f"{type(error).__name__}: {error}"}
 
     if world > 1:
         dist.barrier(device_ids=[local])
