@@ -231,14 +231,12 @@ int rlt_shared_prefix_suffix(const int32_t* block_tables, const int32_t* context
                              int32_t table_width, int32_t page_size, int64_t table_row_stride,
                              void* stream);
 
-/* How the 16-bit shared-prefix chunk kernel stages K/V: 1 (default) =
- * cp.async from the page table; 2 = tiled TMA loads of whole pages into
- * 128-byte-swizzled shared memory where the page size is 8, 16, 32 or 64
- * tokens (cp.async otherwise) -- faster when the chunk phase runs alone
- * (rlt_paged_decode_shared_phases with phases 1), slower beside the suffix
- * decode. Returns the previous choice (any other value only queries). Results
- * agree within rounding (bit-identical for page-aligned chunk starts). No
- * counterpart in the reference. */
+/* How the 16-bit shared-prefix chunk kernel stages K/V: 2 (default) = tiled
+ * TMA loads of whole pages into 128-byte-swizzled shared memory where the
+ * page size is 8, 16, 32 or 64 tokens (cp.async otherwise); 1 = cp.async from
+ * the page table always. Returns the previous choice (any other value only
+ * queries). Results agree within rounding (bit-identical for page-aligned
+ * chunk starts). No counterpart in the reference. */
 int rlt_shared_prefix_select(int32_t staging);
 
 /* Size of the static split-KV scratch of rlt_paged_decode_noalloc (bytes). */

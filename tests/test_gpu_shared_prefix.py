@@ -65,8 +65,8 @@ def test_gqa_and_page_sizes(group, page):
 
 @pytest.fixture(params=[2, 1], ids=["tma", "cp_async"])
 def staging(request):
-    """The chunk kernel's K/V staging (rlt_shared_prefix_select): 1 = cp.async
-    (the default), 2 = tiled TMA loads where the page size allows."""
+    """The chunk kernel's K/V staging (rlt_shared_prefix_select): 2 = tiled
+    TMA loads where the page size allows (the default), 1 = cp.async."""
     lib = _lib.load()
     previous = lib.rlt_shared_prefix_select(request.param)
     yield request.param

@@ -241,7 +241,11 @@ struct LayoutMma {
 template <int D>
 struct LayoutTma {
   static constexpr int kTokens = 64;
-  static constexpr int kStages = 3;
+  // two stages: the next sub-tile lands while one is consumed. Three (108 KB
+  // per CTA) were faster alone but left no room on an SM for the suffix
+  // decode that runs beside this kernel (the call measured 314-340 us
+  // against 253 us with two)
+  static constexpr int kStages = 2;
   static constexpr int kHalves = D / 64;
   static constexpr int kHalfBytes = kTokens * 128;         // 64 tokens x 64 dims x 2 B
   static constexpr int kTileBytes = kHalves * kHalfBytes;  // one K or V sub-tile
@@ -330,9 +334,9 @@ __device__ __forceinline__ uint8_t* align1024(uint8_t* base) {
 // kTma = false: every thread copies its share of each 64-token sub-tile with
 // cp.async from the page table (any page size). kTma = true (pages of 8, 16,
 // 32 or 64 tokens): warp 0's lanes issue one tiled TMA load per page and
-// 64-dim half of K and of V into 128-byte-swizzled stages (three stages, two
-// sub-tiles in flight, bounded mbarrier waits), so no thread spends
-// instructions on copies. The math is the same in both.
+// 64-dim half of K and of V into 128-byte-swizzled stages (double buffered,
+// bounded mbarrier waits), so no thread spends instructions on copies. The
+// math is the same in both.
 template <typename T, int D, bool kTma>
 __global__ void __launch_bounds__(kWarps * 32, 2)
     shared_range_mma_kernel(const __grid_constant__ SharedParams p) {
@@ -867,13 +871,12 @@ int launch(const SharedParams& p, bool tma, int num_chunks, const int32_t* row_s
   return launch_status(cudaGetLastError());
 }
 
-// 1 (default): 16-bit chunks are staged by cp.async; 2: by TMA where the page
-// allows it. TMA staging makes the chunk kernel alone ~8 % faster (configs[1]
-// prefix-cached batch: 87 us against 95 us), but beside the suffix decode the
-// call measured 314-340 us against 261-287 us with cp.async staging (the
-// resident mix of the two kernels' CTAs on an SM differs), so the overlapped
-// call keeps cp.async.
-std::atomic<int> g_shared_staging{1};
+// 2 (default): 16-bit chunks are staged by TMA where the page allows it; 1:
+// always by cp.async. On the configs[1] prefix-cached batch the overlapped
+// call took 253 us with TMA staging against 260 us with cp.async (4096-token
+// chunks; 276 against 284 us with 512-token chunks): the TMA loader spends
+// no instructions per copy.
+std::atomic<int> g_shared_staging{2};
 
 bool aligned16(const void* ptr) { return (reinterpret_cast<uintptr_t>(ptr) & 15u) == 0; }
 
