@@ -41,6 +41,18 @@ def test_backend_rejects_other_architectures(monkeypatch):
         rb.B200PagedAttention(torch.device("cuda"), torch.int8, 128, 16)
 
 
+def test_backend_rejects_head_dims_above_256(monkeypatch):
+    """The reference's dispatcher refuses head_dim > 256 before any launch
+    (vllm_rlt/kernels/paged_attention.py:47-50); so does the backend, on an
+    sm_100a device."""
+    monkeypatch.setattr(torch.version, "hip", None)
+    monkeypatch.setattr(torch.cuda, "get_device_capability", lambda device=None: (10, 0))
+    with pytest.raises(ValueError, match="head_dim"):
+        rb.B200PagedAttention(torch.device("cuda"), torch.bfloat16, 320, 16)
+    with pytest.raises(ValueError, match="head_dim"):
+        rb.B200PagedAttention(torch.device("cuda"), torch.bfloat16, 0, 16)
+
+
 def test_backend_surface(monkeypatch):
     monkeypatch.setattr(torch.version, "hip", None)
     monkeypatch.setattr(torch.cuda, "get_device_capability", lambda device=None: (10, 0))
